@@ -1,0 +1,406 @@
+"""Benchmark of the chunked FP16-accumulate GEMM (f16acc.mm) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the configuration the headline metric is quoted
+on): C = A @ B, M = N = K = 4096, A and B fp16 ~ N(0,1)/sqrt(K)*4 (seeded),
+B row-major, fp16 output, chunked mode (FP16-accumulated 32-long chunks summed
+in FP32, device-side flag + redo).  One step = GEMMS_PER_STEP such products,
+rotating over INPUT_SETS independent (A, B) pairs whose footprint exceeds the
+126 MB L2, so no step reuses L2-resident operands.
+
+Multi-GPU (torchrun, one rank per GPU): M-sharded token batches are
+independent, so every rank runs the same per-GPU work on its own inputs with no
+collective on the data path ("scaling": "weak"); the time is the max over ranks.
+
+--impl reference times the reference's CPU path (the oracle restatement of
+steppergg/f16acc f16acc/kernel.py:37-81: chunked emulation) on the host cores,
+rank 0 only, on a bounded row sample of the same workload.
+
+Prints one JSON line (rank 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+M = N = K = 4096
+GEMMS_PER_STEP = 32
+INPUT_SETS = 4
+METRIC = "TFLOPS @4096^3 FP16 (chunked FP16-accumulate GEMM, f16acc.mm)"
+UNIT = "TFLOPS"
+FALLBACK_PEAK_TFLOPS = 1590.0
+
+
+def flops_per_gemm() -> float:
+    return 2.0 * M * N * K
+
+
+def make_inputs(torch, device, seed, sets):
+    g = torch.Generator(device=device).manual_seed(seed)
+    scale = 4.0 / K ** 0.5
+    out = []
+    for _ in range(sets):
+        a = (torch.randn(M, K, device=device, generator=g) * scale).half()
+        b = (torch.randn(K, N, device=device, generator=g) * scale).half()
+        out.append((a, b))
+    return out
+
+
+# ---------------------------------------------------------------- clocks (NVML)
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting",
+               0x1: "gpu_idle"}
+
+    def __init__(self, index: int, period_s: float = 0.01):
+        self.samples, self.reasons, self.max_mhz, self.ok = [], set(), None, False
+        self.period = period_s
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # NVML missing: report, never guess
+            self.err = repr(e)
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "err", "nvml")}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, cuBLAS bf16 burst)"
+    except Exception:
+        return FALLBACK_PEAK_TFLOPS, "fallback (1.59 PFLOP/s, earlier measurement on this pool)"
+
+
+def profiled_traffic():
+    """DRAM bytes per main-kernel launch from the committed ncu summary, or None."""
+    p = os.path.join(ROOT, "profiles", "tc_gemm_chunked_4096.md")
+    try:
+        for line in open(p):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip()))
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------- distributed plumbing
+def dist_setup(torch, want_nccl: bool):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and want_nccl:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(torch, value: float, world: int, device) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(torch, world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ---------------------------------------------------------------- CPU baseline (oracle)
+def cpu_sample(rows: int, seed: int = 1):
+    import numpy as np
+
+    from oracle import oracle as O
+
+    rng = np.random.default_rng(seed)
+    scale = 4.0 / K ** 0.5
+    a = (rng.standard_normal((rows, K)) * scale).astype(np.float16)
+    b = (rng.standard_normal((K, N)) * scale).astype(np.float16)
+    t0 = time.perf_counter()
+    O.gemm_chunked(a, b, round_every=32)
+    dt = time.perf_counter() - t0
+    return dt, 2.0 * rows * N * K / dt / 1e12
+
+
+def cpu_threads():
+    n = os.environ.get("OMP_NUM_THREADS")
+    return int(n) if n else (os.cpu_count() or 1)
+
+
+def cpu_baseline(target_s: float = 10.0):
+    """Chunked emulation of rows of the 4096^3 product, sized to ~target_s."""
+    dt, _ = cpu_sample(16)
+    rows = int(max(16, min(M, 16 * target_s / max(dt, 1e-3))))
+    dt, tflops = cpu_sample(rows)
+    return {"value": tflops, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+            "sample": f"oracle chunked emulation (oracle/f16acc_oracle.c, OpenMP) of {rows} of the 4096 rows "
+                      f"of one 4096^3 product: {dt:.1f} s"}
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    # size each step so the whole --steps/--warmup run stays within ~2 minutes
+    dt16, _ = cpu_sample(16)
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    rows = int(max(16, min(M, 16 * budget / max(dt16, 1e-3))))
+    for _ in range(args.warmup):
+        cpu_sample(rows)
+    times = []
+    for _ in range(args.steps):
+        dt, _ = cpu_sample(rows)
+        times.append(dt)
+    total = sum(times)
+    value = args.steps * 2.0 * rows * N * K / total / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+        "config": {"workload": "config 2: 4096^3 fp16 GEMM, N(0,1)/sqrt(K)*4, chunked FP16 accumulate",
+                   "rows_per_step": rows},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                         "sample": f"{rows} rows of the 4096^3 product per step (reference chunked semantics, "
+                                   "oracle/f16acc_oracle.c)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+
+    from f16acc_b200 import _lib
+    from f16acc_b200.kernel import mm, mm_phase, plan, tile_flags, workspace_bytes
+
+    world, rank, local = dist_setup(torch, want_nccl=True)
+    if args.gpus != world and world > 1:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
+    stream = torch.cuda.current_stream(dev)
+    variant = {"auto": _lib.VARIANT_AUTO, "tcgen05": _lib.VARIANT_TCGEN05, "mma_sync": _lib.VARIANT_MMA_SYNC}[
+        args.variant]
+
+    sets = make_inputs(torch, dev, seed=1 + rank, sets=INPUT_SETS)
+    outs = [torch.empty(M, N, device=dev, dtype=torch.float16) for _ in range(INPUT_SETS)]
+    wss = [torch.empty(workspace_bytes(M, N, K), device=dev, dtype=torch.uint8) for _ in range(INPUT_SETS)]
+
+    def one(i):
+        a, b = sets[i % INPUT_SETS]
+        mm_phase("main", a, b, outs[i % INPUT_SETS], wss[i % INPUT_SETS], True, variant)
+        mm_phase("redo", a, b, outs[i % INPUT_SETS], wss[i % INPUT_SETS], True, variant)
+
+    def step():
+        for i in range(GEMMS_PER_STEP):
+            one(i)
+
+    # warm-up (also loads modules / sets attributes)
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps, events on the launching stream, barrier + sync both sides
+    clocks = ClockSampler(local)
+    barrier(torch, world)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier(torch, world)
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(torch, ms, world, dev)
+    gemms_total = args.steps * GEMMS_PER_STEP * world
+    value = gemms_total * flops_per_gemm() / (ms_max / 1e3) / 1e12
+    launches = args.steps * GEMMS_PER_STEP * 2
+
+    # ---- roofline: main-kernel duration alone (redo still issued every product)
+    n_main = min(64, max(16, args.steps * 2))
+    main_ms = []
+    for i in range(n_main):
+        a, b = sets[i % INPUT_SETS]
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        mm_phase("main", a, b, outs[i % INPUT_SETS], wss[i % INPUT_SETS], True, variant)
+        e1.record(stream)
+        mm_phase("redo", a, b, outs[i % INPUT_SETS], wss[i % INPUT_SETS], True, variant)
+        main_ms.append((e0, e1))
+    torch.cuda.synchronize()
+    main_avg_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in main_ms)
+    peak, peak_src = measured_peak()
+    achieved = flops_per_gemm() / (main_avg_ms / 1e3) / 1e12
+
+    # ---- accuracy (config 2): max rel err vs FP64, flagged tiles
+    a, b = sets[0]
+    c = mm(a, b)
+    ref = a.double() @ b.double()
+    max_rel = ((c.double() - ref).abs().max() / ref.abs().max()).item()
+    del ref
+    pl = plan(a, b, variant)
+    flagged = int(tile_flags(wss[0], pl).sum().item())
+
+    # ---- cuBLAS on the same box for context (FP32 accumulate and FP16 accumulate)
+    def time_torch(fn, reps=3 * GEMMS_PER_STEP):
+        for i in range(8):
+            fn(i)
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for i in range(reps):
+            fn(i)
+        s1.record(stream)
+        torch.cuda.synchronize()
+        return reps * flops_per_gemm() / (s0.elapsed_time(s1) / 1e3) / 1e12
+
+    mmod = torch.backends.cuda.matmul
+    cublas_f32 = time_torch(lambda i: torch.mm(*sets[i % INPUT_SETS], out=outs[i % INPUT_SETS]))
+    mmod.allow_fp16_accumulation = True
+    try:
+        cublas_f16 = time_torch(lambda i: torch.mm(*sets[i % INPUT_SETS], out=outs[i % INPUT_SETS]))
+    finally:
+        mmod.allow_fp16_accumulation = False
+
+    # ---- e2e through the public API with host buffers (pinned), copies inside the timed region
+    e2e_steps = max(1, min(args.steps, 3))
+    host_in = [(a.cpu().pin_memory(), b.cpu().pin_memory()) for a, b in sets]
+    host_out = [torch.empty(M, N, dtype=torch.float16).pin_memory() for _ in range(INPUT_SETS)]
+    dev_in = [(torch.empty_like(a), torch.empty_like(b)) for a, b in sets]
+    torch.cuda.synchronize()
+    barrier(torch, world)
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record(stream)
+    for _ in range(e2e_steps):
+        for i in range(GEMMS_PER_STEP):
+            j = i % INPUT_SETS
+            dev_in[j][0].copy_(host_in[j][0], non_blocking=True)
+            dev_in[j][1].copy_(host_in[j][1], non_blocking=True)
+            cj = mm(dev_in[j][0], dev_in[j][1])
+            host_out[j].copy_(cj, non_blocking=True)
+    x1.record(stream)
+    torch.cuda.synchronize()
+    barrier(torch, world)
+    e2e_ms = max_over_ranks(torch, x0.elapsed_time(x1), world, dev)
+    e2e_value = e2e_steps * GEMMS_PER_STEP * world * flops_per_gemm() / (e2e_ms / 1e3) / 1e12
+    h2d = GEMMS_PER_STEP * 2 * M * K * 2
+    d2h = GEMMS_PER_STEP * M * N * 2
+
+    line = None
+    if rank == 0:
+        cpu = cpu_baseline() if world == 1 else None
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": "config 2: C = A @ B, 4096^3 fp16, N(0,1)/sqrt(K)*4, B row-major, fp16 out, "
+                                   "chunked FP16 accumulate + device redo",
+                       "gemms_per_step": GEMMS_PER_STEP, "per_gpu": "one 4096-row M shard per product",
+                       "l2": f"inputs rotate over {INPUT_SETS} (A,B) sets = {INPUT_SETS * 64} MiB > 126 MB L2",
+                       "parallelism": f"dp{world} (independent M shards, no collective)",
+                       "variant": args.variant, "kernel": {1: "tcgen05", 2: "mma_sync"}.get(pl["variant"]),
+                       "tile": list(pl["tile"])},
+            "max_rel_err_vs_fp64": max_rel,
+            "flagged_tiles": flagged,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": profiled_traffic(),
+                         "kernel": "main chunked pass", "main_kernel_ms": main_avg_ms, "peak_source": peak_src},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": e2e_steps, "api": "f16acc_b200.mm with pinned host copies"},
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+            "context": {"cublas_f32acc_tflops": cublas_f32, "cublas_f16acc_tflops": cublas_f16,
+                        "reference_published": "65.7 TFLOPS f16acc at 4096^3 on RTX 4060 Ti (README.md:29)"},
+        }
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description="f16acc B200 benchmark")
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--variant", choices=["auto", "tcgen05", "mma_sync"], default="auto")
+    args = ap.parse_args(argv)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

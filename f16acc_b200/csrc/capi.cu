@@ -1,0 +1,343 @@
+// capi.cu -- the C ABI declared in include/f16acc.h: argument checks, kernel
+// choice, TMA descriptors, and the main + redo launches on the caller's stream.
+//
+// Reference host logic (steppergg/f16acc f16acc/kernel.py:84-105): checks
+// (:87-90), output and flag buffers (:93-95), 64-bit indexing (:97-98 -- here
+// always 64-bit address arithmetic, TMA coordinates are 32-bit per dimension),
+// main launch (:99), redo launch on the same stream with no host sync
+// (:100-104).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/f16acc.h"
+#include "launch.h"
+#include "mma_gemm.cuh"
+#include "tc_gemm.cuh"
+
+namespace f16acc {
+
+// Device status word: kernels record the first wait they gave up on here.
+__device__ int g_status = 0;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+    std::once_flag once;
+    cudaError_t err = cudaSuccess;
+    int sms = 0;
+    int* status = nullptr;
+};
+DeviceInfo g_dev[kMaxDevices];
+
+DeviceInfo* device_info(int device) {
+    if (device < 0 || device >= kMaxDevices) return nullptr;
+    DeviceInfo* d = &g_dev[device];
+    std::call_once(d->once, [d, device]() {
+        d->err = cudaDeviceGetAttribute(&d->sms, cudaDevAttrMultiProcessorCount, device);
+        if (d->err != cudaSuccess) return;
+        d->err = cudaGetSymbolAddress(reinterpret_cast<void**>(&d->status), g_status);
+    });
+    return d;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+std::once_flag g_encode_once;
+EncodeTiledFn g_encode = nullptr;
+
+EncodeTiledFn encode_fn() {
+    std::call_once(g_encode_once, []() {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    });
+    return g_encode;
+}
+
+// 2-D FP16 tensor map: inner dimension d0 (contiguous), outer d1 with byte
+// stride stride1, box {b0, b1}, 128-byte swizzle, zero fill out of bounds.
+bool make_map(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t stride1_bytes, uint32_t b0,
+              uint32_t b1) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {d0, d1};
+    const cuuint64_t strides[1] = {stride1_bytes};
+    const cuuint32_t box[2] = {b0, b1};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Operand layout facts the kernel choice needs.  Strides of size-1 dimensions
+// carry no information and are replaced by the natural ones.
+struct Layout {
+    int64_t sAm, sAk, sBk, sBn;
+    bool a_kcontig, a_tma, b_kcontig, b_ncontig, b_tma_k, b_tma_n;
+    bool a_vec, b_kvec, b_nvec;
+};
+
+Layout analyse(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int64_t sBn, int64_t M, int64_t N,
+               int64_t K) {
+    Layout L{};
+    if (K == 1) sAk = 1;
+    if (M == 1) sAm = K;
+    if (K == 1) sBk = N;
+    if (N == 1) sBn = 1;
+    // N == 1 and K == 1 together: B is one element; either view works.
+    L.sAm = sAm; L.sAk = sAk; L.sBk = sBk; L.sBn = sBn;
+    const uintptr_t pa = reinterpret_cast<uintptr_t>(A), pb = reinterpret_cast<uintptr_t>(B);
+    L.a_kcontig = sAk == 1;
+    L.b_kcontig = sBk == 1;
+    L.b_ncontig = sBn == 1;
+    const bool a16 = pa % 16 == 0, b16 = pb % 16 == 0;
+    const uint64_t max_stride = uint64_t(1) << 39;  // TMA byte strides must stay below 2^40
+    L.a_tma = L.a_kcontig && a16 && sAm % 8 == 0 && sAm >= K && uint64_t(sAm) < max_stride;
+    L.b_tma_k = L.b_kcontig && b16 && sBn % 8 == 0 && sBn >= K && uint64_t(sBn) < max_stride;
+    L.b_tma_n = L.b_ncontig && b16 && sBk % 8 == 0 && sBk >= N && uint64_t(sBk) < max_stride;
+    L.a_vec = L.a_kcontig && a16 && sAm % 8 == 0;
+    L.b_kvec = L.b_kcontig && b16 && sBn % 8 == 0;
+    L.b_nvec = L.b_ncontig && b16 && sBk % 8 == 0;
+    return L;
+}
+
+constexpr TcShape kTcShape{128, 2};
+constexpr int kGroupM = 8;
+
+int choose_variant(const Layout& L, int64_t M, int64_t N, int64_t K, int requested) {
+    const bool dims_ok = M < (int64_t(1) << 31) && N < (int64_t(1) << 31) && K < (int64_t(1) << 31);
+    const bool tc_ok = dims_ok && K > 0 && L.a_tma && (L.b_tma_k || L.b_tma_n) && encode_fn() != nullptr;
+    if (requested == F16ACC_VARIANT_TCGEN05) return tc_ok ? F16ACC_VARIANT_TCGEN05 : -1;
+    if (requested == F16ACC_VARIANT_MMA_SYNC) return dims_ok ? F16ACC_VARIANT_MMA_SYNC : -1;
+    if (requested != F16ACC_VARIANT_AUTO) return -1;
+    if (tc_ok) return F16ACC_VARIANT_TCGEN05;
+    return dims_ok ? F16ACC_VARIANT_MMA_SYNC : -1;
+}
+
+// Which of the two launches run() makes: the main pass writes C and the
+// flags, the redo pass recomputes flagged tiles (kernel.py:99 and :100-104).
+constexpr int kPhaseMain = 1, kPhaseRedo = 2, kPhaseBoth = 3;
+
+struct DeviceGuard {
+    int prev = -1;
+    bool switched = false;
+    cudaError_t err = cudaSuccess;
+    explicit DeviceGuard(int device) {
+        err = cudaGetDevice(&prev);
+        if (err == cudaSuccess && prev != device) {
+            err = cudaSetDevice(device);
+            switched = err == cudaSuccess;
+        }
+    }
+    ~DeviceGuard() {
+        if (switched) cudaSetDevice(prev);
+    }
+};
+
+int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int64_t sBn, void* C, int64_t sCm,
+        int64_t sCn, int c_dtype, int64_t M, int64_t N, int64_t K, int chunked, void* workspace, size_t ws_bytes,
+        int device, void* stream_ptr, int variant, int phases) {
+    if (M < 0 || N < 0 || K < 0) return F16ACC_ERR_INVALID_ARGUMENT;
+    if (c_dtype != F16ACC_OUT_F16 && c_dtype != F16ACC_OUT_F32 && c_dtype != F16ACC_OUT_BF16)
+        return F16ACC_ERR_INVALID_ARGUMENT;
+    if (M == 0 || N == 0) return F16ACC_OK;
+    if (C == nullptr) return F16ACC_ERR_INVALID_ARGUMENT;
+    if (M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31) || K >= (int64_t(1) << 31))
+        return F16ACC_ERR_INVALID_ARGUMENT;
+    DeviceInfo* info = device_info(device);
+    if (!info) return F16ACC_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess || info->err != cudaSuccess) return F16ACC_ERR_CUDA;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+
+    if (K == 0) {  // empty sum: C = 0, nothing to flag
+        if (!(phases & kPhaseMain)) return F16ACC_OK;
+        return launch_fill_zero(C, sCm, sCn, int(M), int(N), c_dtype, stream) == cudaSuccess ? F16ACC_OK
+                                                                                             : F16ACC_ERR_CUDA;
+    }
+    if (A == nullptr || B == nullptr) return F16ACC_ERR_INVALID_ARGUMENT;
+    const Layout L = analyse(A, sAm, sAk, B, sBk, sBn, M, N, K);
+    int v = choose_variant(L, M, N, K, variant);
+    if (v < 0) return variant == F16ACC_VARIANT_AUTO ? F16ACC_ERR_INVALID_ARGUMENT : F16ACC_ERR_UNSUPPORTED;
+    if (chunked) {
+        if (workspace == nullptr || ws_bytes < f16acc_workspace_bytes(M, N, K) ||
+            reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
+            return F16ACC_ERR_WORKSPACE;
+    }
+    const int esize = c_dtype == F16ACC_OUT_F32 ? 4 : 2;
+    const uintptr_t pc = reinterpret_cast<uintptr_t>(C);
+
+    TcParams p;
+    std::memset(&p, 0, sizeof(p));
+    const bool b_mn = !L.b_tma_k;
+    if (v == F16ACC_VARIANT_TCGEN05) {
+        const int bn = kTcShape.bn;
+        const bool maps_ok =
+            make_map(&p.tmA, A, uint64_t(K), uint64_t(M), uint64_t(L.sAm) * 2, 64, 128) &&
+            (b_mn ? make_map(&p.tmB, B, uint64_t(N), uint64_t(K), uint64_t(L.sBk) * 2, 64, 64)
+                  : make_map(&p.tmB, B, uint64_t(K), uint64_t(N), uint64_t(L.sBn) * 2, 64, bn));
+        if (!maps_ok) {
+            if (variant != F16ACC_VARIANT_AUTO) return F16ACC_ERR_UNSUPPORTED;
+            v = F16ACC_VARIANT_MMA_SYNC;  // the descriptor encoder refused these operands
+        }
+    }
+    if (v == F16ACC_VARIANT_TCGEN05) {
+        const int bn = kTcShape.bn;
+        p.C = C;
+        p.sCm = sCm;
+        p.sCn = sCn;
+        p.M = int(M);
+        p.N = int(N);
+        p.K = int(K);
+        p.tiles_m = int(cdiv(M, 128));
+        p.tiles_n = int(cdiv(N, bn));
+        p.group_m = kGroupM;
+        p.c_vec = (sCn == 1 && pc % 16 == 0 && (sCm * esize) % 16 == 0) ? 1 : 0;
+        p.flags = static_cast<uint8_t*>(workspace);
+        p.status = info->status;
+        const int64_t tiles = int64_t(p.tiles_m) * p.tiles_n;
+        const int grid = int(tiles < info->sms ? tiles : info->sms);
+        if ((phases & kPhaseMain) &&
+            launch_tc(p, kTcShape, chunked != 0, b_mn, c_dtype, false, grid, stream) != cudaSuccess)
+            return F16ACC_ERR_CUDA;
+        if (chunked && (phases & kPhaseRedo) &&
+            launch_tc(p, kTcShape, false, b_mn, c_dtype, true, grid, stream) != cudaSuccess)
+            return F16ACC_ERR_CUDA;
+        return F16ACC_OK;
+    }
+
+    MmaParams q;
+    std::memset(&q, 0, sizeof(q));
+    q.A = static_cast<const __half*>(A);
+    q.B = static_cast<const __half*>(B);
+    q.C = C;
+    q.sAm = L.sAm;
+    q.sAk = L.sAk;
+    q.sBk = L.sBk;
+    q.sBn = L.sBn;
+    q.sCm = sCm;
+    q.sCn = sCn;
+    q.M = int(M);
+    q.N = int(N);
+    q.K = int(K);
+    q.tiles_m = int(cdiv(M, MmaCfg::BM));
+    q.tiles_n = int(cdiv(N, MmaCfg::BN));
+    q.group_m = kGroupM;
+    q.c_vec = (sCn == 1 && pc % (2 * esize) == 0 && sCm % 2 == 0) ? 1 : 0;
+    q.flags = static_cast<uint8_t*>(workspace);
+    const int a_mode = L.a_vec ? kLoadKVec : kLoadGeneric;
+    const int b_mode = L.b_kvec ? kLoadKVec : (L.b_nvec ? kLoadNVec : kLoadGeneric);
+    const int64_t tiles = int64_t(q.tiles_m) * q.tiles_n;
+    if (tiles >= (int64_t(1) << 31)) return F16ACC_ERR_INVALID_ARGUMENT;
+    if ((phases & kPhaseMain) &&
+        launch_mma(q, chunked != 0, a_mode, b_mode, c_dtype, false, int(tiles), stream) != cudaSuccess)
+        return F16ACC_ERR_CUDA;
+    if (chunked && (phases & kPhaseRedo)) {
+        const int64_t redo_grid = tiles < 2 * info->sms ? tiles : 2 * info->sms;
+        if (launch_mma(q, false, a_mode, b_mode, c_dtype, true, int(redo_grid), stream) != cudaSuccess)
+            return F16ACC_ERR_CUDA;
+    }
+    return F16ACC_OK;
+}
+
+}  // namespace
+}  // namespace f16acc
+
+using namespace f16acc;
+
+extern "C" {
+
+int f16acc_gemm(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int64_t sBn, void* C,
+                int64_t sCm, int64_t sCn, int c_dtype, int64_t M, int64_t N, int64_t K, int chunked, void* workspace,
+                size_t ws_bytes, int device, void* stream) {
+    return run(A, sAm, sAk, B, sBk, sBn, C, sCm, sCn, c_dtype, M, N, K, chunked, workspace, ws_bytes, device, stream,
+               F16ACC_VARIANT_AUTO, kPhaseBoth);
+}
+
+int f16acc_gemm_ex(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int64_t sBn, void* C,
+                   int64_t sCm, int64_t sCn, int c_dtype, int64_t M, int64_t N, int64_t K, int chunked,
+                   void* workspace, size_t ws_bytes, int device, void* stream, int variant) {
+    return run(A, sAm, sAk, B, sBk, sBn, C, sCm, sCn, c_dtype, M, N, K, chunked, workspace, ws_bytes, device, stream,
+               variant, kPhaseBoth);
+}
+
+int f16acc_gemm_main(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int64_t sBn, void* C,
+                     int64_t sCm, int64_t sCn, int c_dtype, int64_t M, int64_t N, int64_t K, int chunked,
+                     void* workspace, size_t ws_bytes, int device, void* stream, int variant) {
+    return run(A, sAm, sAk, B, sBk, sBn, C, sCm, sCn, c_dtype, M, N, K, chunked, workspace, ws_bytes, device, stream,
+               variant, kPhaseMain);
+}
+
+int f16acc_gemm_redo(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int64_t sBn, void* C,
+                     int64_t sCm, int64_t sCn, int c_dtype, int64_t M, int64_t N, int64_t K, int chunked,
+                     void* workspace, size_t ws_bytes, int device, void* stream, int variant) {
+    return run(A, sAm, sAk, B, sBk, sBn, C, sCm, sCn, c_dtype, M, N, K, chunked, workspace, ws_bytes, device, stream,
+               variant, kPhaseRedo);
+}
+
+size_t f16acc_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+    (void)K;
+    if (M <= 0 || N <= 0) return 16;
+    // Smallest tile any variant uses is 128 x 128.
+    const int64_t tiles = cdiv(M, 128) * cdiv(N, 128);
+    return size_t(tiles) * kFlagBytesPerTile;
+}
+
+const char* f16acc_strerror(int code) {
+    switch (code) {
+        case F16ACC_OK: return "ok";
+        case F16ACC_ERR_INVALID_ARGUMENT:
+            return "mm needs (M, K) @ (K, N) fp16 operands with non-negative sizes below 2**31 and a supported output dtype";
+        case F16ACC_ERR_WORKSPACE: return "workspace missing, smaller than f16acc_workspace_bytes(), or not 16-byte aligned";
+        case F16ACC_ERR_UNSUPPORTED: return "the requested kernel variant cannot take these operands";
+        case F16ACC_ERR_CUDA: return "a CUDA call or kernel launch failed";
+        case F16ACC_ERR_DEVICE_TIMEOUT: return "a kernel gave up waiting on the device (see f16acc_device_status)";
+    }
+    return "unknown f16acc error code";
+}
+
+int f16acc_get_plan(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int64_t sBn, int64_t M,
+                    int64_t N, int64_t K, int variant, f16acc_plan* out) {
+    if (!out || M < 0 || N < 0 || K < 0) return F16ACC_ERR_INVALID_ARGUMENT;
+    const Layout L = analyse(A, sAm, sAk, B, sBk, sBn, M, N, K);
+    const int v = choose_variant(L, M, N, K, variant);
+    if (v < 0) return variant == F16ACC_VARIANT_AUTO ? F16ACC_ERR_INVALID_ARGUMENT : F16ACC_ERR_UNSUPPORTED;
+    out->variant = v;
+    out->tile_m = 128;
+    out->tile_n = v == F16ACC_VARIANT_TCGEN05 ? kTcShape.bn : MmaCfg::BN;
+    out->tiles_m = cdiv(M, out->tile_m);
+    out->tiles_n = cdiv(N, out->tile_n);
+    return F16ACC_OK;
+}
+
+int f16acc_flag_bytes_per_tile(void) { return kFlagBytesPerTile; }
+
+int f16acc_device_status(int device, int reset) {
+    DeviceInfo* info = device_info(device);
+    if (!info || info->err != cudaSuccess) return -1;
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return -1;
+    if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+    int v = 0;
+    if (cudaMemcpy(&v, info->status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (reset) {
+        const int zero = 0;
+        if (cudaMemcpy(info->status, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) return -1;
+    }
+    return v;
+}
+
+const char* f16acc_version(void) { return "f16acc_b200 0.1 (sm_100a: tcgen05 + mma.sync)"; }
+
+}  // extern "C"

@@ -1,0 +1,54 @@
+// launch.h -- host-side launch entry points of the kernel translation units
+// (one nvcc process per unit so the template instantiations build in parallel).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace f16acc {
+
+struct TcParams;
+struct MmaParams;
+
+// tcgen05 kernel: BN output columns per tile (128 or 256), EPI_SPLIT column
+// slices per TMEM lane quarter.  `redo` selects the FP32 pass over flagged
+// tiles (requires chunked == false) launched with programmatic stream
+// serialisation.
+struct TcShape {
+    int bn;
+    int epi_split;
+};
+int tc_threads(TcShape shape);
+int tc_smem_bytes(TcShape shape);
+bool tc_shape_supported(TcShape shape);
+cudaError_t launch_tc(const TcParams& p, TcShape shape, bool chunked, bool b_mn, int out, bool redo, int grid,
+                      cudaStream_t stream);
+
+// mma.sync kernel: a_mode / b_mode from LoadMode.
+cudaError_t launch_mma(const MmaParams& p, bool chunked, int a_mode, int b_mode, int out, bool redo, int grid,
+                       cudaStream_t stream);
+cudaError_t launch_fill_zero(void* C, int64_t sCm, int64_t sCn, int M, int N, int out, cudaStream_t stream);
+
+// Launch helper: cudaLaunchKernelEx with optional programmatic stream
+// serialisation (the dependent kernel may start its prologue while the
+// previous kernel on the stream drains; it calls griddepcontrol.wait before
+// touching that kernel's results).
+template <typename Kernel, typename Params>
+cudaError_t launch_ex(Kernel kernel, const Params& p, int grid, int threads, int smem, cudaStream_t stream, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
+}  // namespace f16acc

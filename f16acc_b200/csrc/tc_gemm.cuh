@@ -1,0 +1,307 @@
+// tc_gemm.cuh -- warp-specialised tcgen05 GEMM for sm_100a, chunked FP16
+// accumulate with FP32 chunk sums, plus its FP32-accumulate twin that serves
+// both `chunked=False` and the redo of flagged tiles.
+//
+// Reference semantics (steppergg/f16acc):
+//   f16acc/kernel.py:44-49  K walked in 32-long chunks from absolute offset 0;
+//                           each chunk is a dot with an FP16 accumulator,
+//                           converted to FP32 and added to an FP32 total.
+//   f16acc/kernel.py:50-51  FP32 mode: one FP32 accumulator over all of K.
+//   f16acc/kernel.py:70-71  tile flag = any accumulator not finite.
+//   f16acc/kernel.py:75-81  redo: flagged tiles recomputed in FP32 mode.
+//
+// Design (one persistent CTA per SM, 128 x BN output tile, 1-CTA UMMA):
+//   warp 0      TMA producer: A [128 x 64] and B [BN x 64] (or [64 x BN] when B
+//               is N-contiguous) per stage into a STAGES-deep smem ring,
+//               128-byte swizzle, completion counted on full[s].
+//   warp 1      TMEM owner + MMA issuer (one lane).  Chunked mode: per 32-long
+//               chunk, two K=16 tcgen05.mma kind::f16 with an FP16 D into one
+//               of NBUF TMEM buffers (first with accumulate off), then
+//               tcgen05.commit -> tfull[b].  FP32 mode: the whole K loop into
+//               one FP32 TMEM buffer per tile.
+//   warps 2..   epilogue, 4*EPI_SPLIT warps: warp w reads TMEM lanes
+//               32*(w%4).. (its lane quarter) and a CW = BN/EPI_SPLIT column
+//               slice.  Chunked mode: per chunk tcgen05.ld (FP16 pairs packed),
+//               release the buffer, then one mixed-precision FP32 add per
+//               element into register accumulators; at tile end a non-finite
+//               probe sets the tile's flag slot and the row slice is stored.
+// No cluster multicast anywhere; every load reads this GPU's own memory.
+#pragma once
+
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace f16acc {
+
+struct TcParams {
+    CUtensorMap tmA;  // A [M, K], K contiguous: dims {K, M}, box {64, 128}
+    CUtensorMap tmB;  // B K-contiguous: dims {K, N}, box {64, BN};  N-contiguous: dims {N, K}, box {64, 64}
+    void* C;
+    int64_t sCm, sCn;
+    int M, N, K;
+    int tiles_m, tiles_n;
+    int group_m;
+    int c_vec;        // C rows allow 16-byte vector stores
+    uint8_t* flags;   // kFlagBytesPerTile per tile
+    int* status;      // device status word (timeouts)
+};
+
+template <int BN_, int EPI_SPLIT_>
+struct TcConfig {
+    static constexpr int BM = 128;
+    static constexpr int BN = BN_;
+    static constexpr int BK = 64;  // one 128-byte swizzle row of f16 = two 32-long chunks
+    static constexpr int EPI_SPLIT = EPI_SPLIT_;
+    static constexpr int EPI_WARPS = 4 * EPI_SPLIT;
+    static constexpr int CW = BN / EPI_SPLIT;  // columns per epilogue warp
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = (BN == 256) ? 4 : 6;
+    static constexpr int TMEM_COLS = 512;
+    static constexpr int ACC_COLS = BN;  // one 32-bit TMEM column per accumulator element, f16 or f32
+    static constexpr int NBUF = TMEM_COLS / ACC_COLS;
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*alignment slack*/ + BAR_BYTES;
+    static_assert(EPI_WARPS * 2 <= kFlagBytesPerTile, "flag slot holds two bytes per epilogue warp");
+    static_assert(CW == 32 || CW % 64 == 0, "epilogue column slice");
+    static_assert((2 * STAGES + 2 * NBUF + 1) * 8 + 16 <= BAR_BYTES, "barrier area");
+};
+
+template <int BN, int EPI_SPLIT, bool CHUNKED, bool B_MN, int OUT, bool REDO>
+__global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT>::THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ TcParams p) {
+    using Cfg = TcConfig<BN, EPI_SPLIT>;
+    constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES, NBUF = Cfg::NBUF, CW = Cfg::CW;
+    static_assert(!(CHUNKED && REDO), "the redo pass runs in FP32 mode");
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + NBUF;
+    uint64_t* drain = tempty + NBUF;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < NBUF; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], Cfg::EPI_WARPS);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbarrier_init();
+        tma_prefetch_desc(&p.tmA);
+        tma_prefetch_desc(&p.tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if constexpr (REDO) {
+        grid_dep_wait();  // flags and C come from the main pass
+    } else {
+        grid_dep_launch();  // let the redo pass get scheduled as early as possible
+    }
+
+    const int tiles = p.tiles_m * p.tiles_n;
+    const int nkb = (p.K + BK - 1) / BK;
+    const int nchunks = (p.K + 31) / 32;
+    const int nk16 = (p.K + 15) / 16;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t s = 0, ph = 0;
+            uint32_t pending = 0, pend_parity = 0;  // stages with a load issued, and that load's phase parity
+            for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+                int tm, tn;
+                raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+                if (REDO && !tile_flagged(p.flags, static_cast<int64_t>(tm) * p.tiles_n + tn)) continue;
+                for (int kb = 0; kb < nkb; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.status, kStatusTimeoutProducer)) goto producer_done;
+                    mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+                    pending |= 1u << s;
+                    pend_parity = (pend_parity & ~(1u << s)) | (ph << s);
+                    tma_load_2d(sA + s * Cfg::A_BYTES, &p.tmA, &full[s], kb * BK, tm * BM);
+                    if constexpr (!B_MN) {
+                        tma_load_2d(sB + s * Cfg::B_BYTES, &p.tmB, &full[s], kb * BK, tn * BN);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < BN / 64; ++j)
+                            tma_load_2d(sB + s * Cfg::B_BYTES + j * (64 * BK * 2), &p.tmB, &full[s], tn * BN + j * 64,
+                                        kb * BK);
+                    }
+                    if (++s == STAGES) { s = 0; ph ^= 1u; }
+                }
+            }
+        producer_done:
+            // Let every copy this CTA issued land before the CTA can exit
+            // (they already have on a normal exit; this matters after an abort).
+            for (int st = 0; st < STAGES; ++st)
+                if (pending & (1u << st)) mbar_wait_drain(&full[st], (pend_parity >> st) & 1u);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16(!CHUNKED, B_MN, BM, BN);
+            const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
+            uint32_t s = 0, ph = 0, b = 0, tph = 0;
+            for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+                int tm, tn;
+                raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+                if (REDO && !tile_flagged(p.flags, static_cast<int64_t>(tm) * p.tiles_n + tn)) continue;
+                if constexpr (CHUNKED) {
+                    for (int kb = 0; kb < nkb; ++kb) {
+                        if (!mbar_wait(&full[s], ph, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
+                        tc_fence_after();
+#pragma unroll
+                        for (int cc = 0; cc < 2; ++cc) {
+                            const int c = kb * 2 + cc;
+                            if (c >= nchunks) break;
+                            if (!mbar_wait(&tempty[b], tph ^ 1u, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
+                            tc_fence_after();
+                            const uint32_t d = tmem + b * Cfg::ACC_COLS;
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const int ks = cc * 2 + h;
+                                if (h == 1 && c * 32 + 16 >= p.K) break;  // K16 step past the end adds nothing
+                                const uint64_t ad = sdesc_sw128(sA0 + s * Cfg::A_BYTES + ks * 32, 16, 1024);
+                                const uint64_t bd = B_MN ? sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 2048, 64 * BK * 2, 1024)
+                                                         : sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 32, 16, 1024);
+                                umma_f16(d, ad, bd, idesc, h);
+                            }
+                            umma_commit(&tfull[b]);
+                            if (++b == NBUF) { b = 0; tph ^= 1u; }
+                        }
+                        umma_commit(&empty[s]);
+                        if (++s == STAGES) { s = 0; ph ^= 1u; }
+                    }
+                } else {
+                    if (!mbar_wait(&tempty[b], tph ^ 1u, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
+                    tc_fence_after();
+                    const uint32_t d = tmem + b * Cfg::ACC_COLS;
+                    for (int kb = 0; kb < nkb; ++kb) {
+                        if (!mbar_wait(&full[s], ph, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
+                        tc_fence_after();
+#pragma unroll
+                        for (int ks = 0; ks < BK / 16; ++ks) {
+                            const int k16 = kb * (BK / 16) + ks;
+                            if (k16 >= nk16) break;
+                            const uint64_t ad = sdesc_sw128(sA0 + s * Cfg::A_BYTES + ks * 32, 16, 1024);
+                            const uint64_t bd = B_MN ? sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 2048, 64 * BK * 2, 1024)
+                                                     : sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 32, 16, 1024);
+                            umma_f16(d, ad, bd, idesc, k16 > 0 ? 1u : 0u);
+                        }
+                        umma_commit(&empty[s]);
+                        if (++s == STAGES) { s = 0; ph ^= 1u; }
+                    }
+                    umma_commit(&tfull[b]);
+                    if (++b == NBUF) { b = 0; tph ^= 1u; }
+                }
+            }
+        mma_done:
+            // All MMAs issued by this thread complete before TMEM is freed.
+            umma_commit(drain);
+            mbar_wait_drain(drain, 0);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int e = warp - 2;          // epilogue warp index
+        const int q = warp & 3;          // TMEM lane quarter this warp may access
+        const int colg = e >> 2;         // column slice
+        const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+        uint32_t b = 0, tph = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+            int tm, tn;
+            raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+            const int64_t tile_id = static_cast<int64_t>(tm) * p.tiles_n + tn;
+            if (REDO && !tile_flagged(p.flags, tile_id)) continue;
+            float acc[CW];
+            bool ok = true;
+            if constexpr (CHUNKED) {
+#pragma unroll
+                for (int j = 0; j < CW; ++j) acc[j] = 0.0f;
+                for (int c = 0; c < nchunks; ++c) {
+                    ok = mbar_wait(&tfull[b], tph, abort_flag, p.status, kStatusTimeoutEpilogue);
+                    if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t taddr = tmem + lane_base + b * Cfg::ACC_COLS + colg * CW;
+                    if constexpr (CW == 32) {
+                        uint32_t r[16];
+                        tmem_ld_32x32b_x16_pack16(taddr, r);
+                        tmem_wait_ld();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[b]);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) add_f16x2_to_f32(acc[2 * i], acc[2 * i + 1], r[i]);
+                    } else {
+                        uint32_t r[CW / 2];
+#pragma unroll
+                        for (int j = 0; j < CW / 64; ++j)
+                            tmem_ld_32x32b_x32_pack16(taddr + j * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[j * 32]));
+                        tmem_wait_ld();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[b]);
+#pragma unroll
+                        for (int i = 0; i < CW / 2; ++i) add_f16x2_to_f32(acc[2 * i], acc[2 * i + 1], r[i]);
+                    }
+                    if (++b == NBUF) { b = 0; tph ^= 1u; }
+                }
+                if (!ok) break;
+                float z = 0.0f;
+#pragma unroll
+                for (int j = 0; j < CW; ++j) z = nonfinite_probe(z, acc[j]);
+                const bool bad = __any_sync(0xffffffffu, z != z);
+                if (lane == 0)
+                    *reinterpret_cast<uint16_t*>(p.flags + tile_id * kFlagBytesPerTile + 2 * e) = bad ? 1 : 0;
+            } else {
+                ok = mbar_wait(&tfull[b], tph, abort_flag, p.status, kStatusTimeoutEpilogue);
+                if (!__all_sync(0xffffffffu, ok)) break;
+                tc_fence_after();
+                const uint32_t taddr = tmem + lane_base + b * Cfg::ACC_COLS + colg * CW;
+#pragma unroll
+                for (int j = 0; j < CW / 32; ++j) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + j * 32, r);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) acc[j * 32 + i] = __uint_as_float(r[i]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[b]);
+                if (++b == NBUF) { b = 0; tph ^= 1u; }
+            }
+            const int row = tm * BM + q * 32 + lane;
+            const int col0 = tn * BN + colg * CW;
+            store_row<OUT, CW>(p.C, p.sCm, p.sCn, row, col0, p.M, p.N, acc, p.c_vec != 0);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
+}
+
+}  // namespace f16acc

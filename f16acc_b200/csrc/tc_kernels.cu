@@ -1,0 +1,79 @@
+// tc_kernels.cu -- instantiations and launchers of the tcgen05 GEMM kernel.
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "launch.h"
+#include "tc_gemm.cuh"
+
+namespace f16acc {
+
+namespace {
+
+// cudaFuncSetAttribute is per function and device; do it once for each pair.
+std::mutex g_attr_mu;
+std::set<std::pair<const void*, int>> g_attr_done;
+
+template <typename Kernel>
+cudaError_t ensure_smem_attr(Kernel kernel, int smem) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const void* key = reinterpret_cast<const void*>(kernel);
+    std::lock_guard<std::mutex> lock(g_attr_mu);
+    if (g_attr_done.count({key, dev})) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess) g_attr_done.insert({key, dev});
+    return e;
+}
+
+template <int BN, int EPI, bool CHUNKED, bool B_MN, int OUT, bool REDO>
+cudaError_t launch_one(const TcParams& p, int grid, cudaStream_t stream) {
+    using Cfg = TcConfig<BN, EPI>;
+    auto kernel = tc_gemm_kernel<BN, EPI, CHUNKED, B_MN, OUT, REDO>;
+    cudaError_t e = ensure_smem_attr(kernel, Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    return launch_ex(kernel, p, grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream, /*pdl=*/REDO);
+}
+
+template <int BN, int EPI, bool B_MN, int OUT>
+cudaError_t launch_mode(const TcParams& p, bool chunked, bool redo, int grid, cudaStream_t stream) {
+    if (redo) return launch_one<BN, EPI, false, B_MN, OUT, true>(p, grid, stream);
+    if (chunked) return launch_one<BN, EPI, true, B_MN, OUT, false>(p, grid, stream);
+    return launch_one<BN, EPI, false, B_MN, OUT, false>(p, grid, stream);
+}
+
+template <int BN, int EPI>
+cudaError_t launch_shape(const TcParams& p, bool chunked, bool b_mn, int out, bool redo, int grid, cudaStream_t stream) {
+    if (b_mn) {
+        switch (out) {
+            case kOutF16: return launch_mode<BN, EPI, true, kOutF16>(p, chunked, redo, grid, stream);
+            case kOutF32: return launch_mode<BN, EPI, true, kOutF32>(p, chunked, redo, grid, stream);
+            case kOutBF16: return launch_mode<BN, EPI, true, kOutBF16>(p, chunked, redo, grid, stream);
+        }
+    } else {
+        switch (out) {
+            case kOutF16: return launch_mode<BN, EPI, false, kOutF16>(p, chunked, redo, grid, stream);
+            case kOutF32: return launch_mode<BN, EPI, false, kOutF32>(p, chunked, redo, grid, stream);
+            case kOutBF16: return launch_mode<BN, EPI, false, kOutBF16>(p, chunked, redo, grid, stream);
+        }
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+bool tc_shape_supported(TcShape s) { return s.bn == 128 && s.epi_split == 2; }
+
+int tc_threads(TcShape s) { return s.bn == 128 && s.epi_split == 2 ? TcConfig<128, 2>::THREADS : 0; }
+
+int tc_smem_bytes(TcShape s) { return s.bn == 128 && s.epi_split == 2 ? TcConfig<128, 2>::SMEM_BYTES : 0; }
+
+cudaError_t launch_tc(const TcParams& p, TcShape shape, bool chunked, bool b_mn, int out, bool redo, int grid,
+                      cudaStream_t stream) {
+    if (shape.bn == 128 && shape.epi_split == 2)
+        return launch_shape<128, 2>(p, chunked, b_mn, out, redo, grid, stream);
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace f16acc

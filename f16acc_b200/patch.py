@@ -1,0 +1,41 @@
+"""Route FP16 nn.Linear through the chunked FP16-accumulate GEMM.
+
+    import f16acc_b200 as f16acc; f16acc.enable()
+
+Behaviour of steppergg/f16acc f16acc/patch.py:17-40, kept as is: only
+F.linear is replaced (every nn.Linear calls it).  Inputs that are not fp16 on
+CUDA, need gradients, or have fewer than MIN_ROWS rows (token-by-token
+decode, memory bound) go to the original F.linear (cuBLAS).  FP16 chunk
+overflow is handled on the device (the tile is redone with FP32 accumulation),
+so there is no host sync per call.
+"""
+
+import torch
+import torch.nn.functional as F
+
+from .kernel import mm
+
+MIN_ROWS = 128
+_orig = F.linear
+calls = {"chunked": 0, "original": 0}
+
+
+def linear(x, w, b=None):
+    rows = x.shape[:-1].numel()
+    if not (x.is_cuda and x.dtype == w.dtype == torch.float16 and rows >= MIN_ROWS and not torch.is_grad_enabled()):
+        calls["original"] += 1
+        return _orig(x, w, b)
+    x2 = x.reshape(rows, x.shape[-1])
+    y = mm(x2, w.t())  # [K, N] view of the [N, K] weight: K-contiguous B, no copy
+    if b is not None:
+        y += b
+    calls["chunked"] += 1
+    return y.view(*x.shape[:-1], w.shape[0])
+
+
+def enable():
+    F.linear = linear  # nn.Linear calls F.linear through this same module
+
+
+def disable():
+    F.linear = _orig

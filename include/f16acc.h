@@ -1,0 +1,138 @@
+/*
+ * f16acc.h -- C ABI of the B200 (sm_100a) chunked FP16-accumulate GEMM.
+ *
+ * C = A @ B with FP16 operands.  K is walked in 32-long chunks from offset 0;
+ * each chunk is accumulated in FP16 on the tensor cores and added into an
+ * FP32 accumulator.  Tiles whose FP16 chunk overflowed (any accumulator not
+ * finite at the end) are flagged on the device and recomputed with FP32
+ * accumulation by a second launch on the same stream, with no host sync.
+ *
+ * Plain C: pointers, element strides, sizes; no CUDA or framework types.
+ * `stream` is a cudaStream_t (NULL = legacy default stream) on `device`.
+ * All calls are asynchronous on that stream and never abort the process:
+ * they return F16ACC_OK or an error code (f16acc_strerror).
+ *
+ * Reference interface replaced (steppergg/f16acc, file:line in that project):
+ *   f16acc/kernel.py:84-105   mm(a, b, out_dtype=torch.float16, chunked=True)
+ *     -> f16acc_gemm (checks :87-90, output + flag buffers :93-95, the 64-bit
+ *        index choice :97-98, the `_gemm` launch :99 and the `_redo` launch
+ *        :100-104 all happen behind this one call; C and the workspace are
+ *        caller-owned here instead of allocated inside).
+ *   f16acc/kernel.py:94-95    the int8 flag buffer sized for the smallest tile
+ *     -> f16acc_workspace_bytes.
+ *   f16acc/kernel.py:87-90    ValueError messages -> f16acc_strerror.
+ */
+#ifndef F16ACC_H_
+#define F16ACC_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes. */
+#define F16ACC_OK 0
+#define F16ACC_ERR_INVALID_ARGUMENT 1 /* shapes, strides, dtype code, null pointers */
+#define F16ACC_ERR_WORKSPACE 2        /* workspace too small or misaligned */
+#define F16ACC_ERR_UNSUPPORTED 3      /* forced variant cannot take these operands */
+#define F16ACC_ERR_CUDA 4             /* a CUDA runtime call or launch failed */
+#define F16ACC_ERR_DEVICE_TIMEOUT 5   /* a kernel gave up on a wait (see f16acc_device_status) */
+
+/* Output element types (c_dtype); kernel.py:93 allocates C as out_dtype. */
+#define F16ACC_OUT_F16 0
+#define F16ACC_OUT_F32 1
+#define F16ACC_OUT_BF16 2
+
+/* Kernel variants for f16acc_gemm_ex (measurement and tests). */
+#define F16ACC_VARIANT_AUTO 0     /* tcgen05 when the operands allow TMA, else mma.sync */
+#define F16ACC_VARIANT_TCGEN05 1  /* warp-specialised tcgen05/TMA kernel only */
+#define F16ACC_VARIANT_MMA_SYNC 2 /* warp-level mma.sync kernel (any strides) */
+
+/*
+ * C[M,N] = A[M,K] @ B[K,N].  Replaces kernel.py:84-105 `mm`.
+ *   A, B     FP16 device pointers; element (i,k) of A at A + i*sAm + k*sAk,
+ *            element (k,j) of B at B + k*sBk + j*sBn (strides in elements,
+ *            any values: row-major, transposed views such as w.t(), padded rows).
+ *   C        device pointer, element (i,j) at C + i*sCm + j*sCn, type c_dtype.
+ *   chunked  1: chunked FP16 accumulate + flag + redo (kernel.py:48-49,70-71,75-81);
+ *            0: plain FP32 accumulate (kernel.py:50-51).
+ *   workspace, ws_bytes  device scratch of at least f16acc_workspace_bytes(M,N,K)
+ *            bytes, 16-byte aligned; holds the per-tile overflow flags.  It may
+ *            be uninitialised and must stay untouched until the call's work on
+ *            `stream` is done.  Unused (may be NULL) when chunked == 0.
+ *   device   CUDA ordinal that owns A, B, C and the workspace.
+ * K == 0 writes zeros; M == 0 or N == 0 does nothing.
+ */
+int f16acc_gemm(const void *A, int64_t sAm, int64_t sAk,
+                const void *B, int64_t sBk, int64_t sBn,
+                void *C, int64_t sCm, int64_t sCn, int c_dtype,
+                int64_t M, int64_t N, int64_t K, int chunked,
+                void *workspace, size_t ws_bytes, int device, void *stream);
+
+/* Bytes of workspace f16acc_gemm needs for an M x N x K product (kernel.py:94-95:
+ * sized for the smallest tile any variant uses). */
+size_t f16acc_workspace_bytes(int64_t M, int64_t N, int64_t K);
+
+/* Static message for a return code (the ValueError texts of kernel.py:87-90). */
+const char *f16acc_strerror(int code);
+
+/* ---- additions with no counterpart in the reference ---------------------- */
+
+/* f16acc_gemm with a forced kernel variant (F16ACC_VARIANT_*): the warp-level
+ * mma.sync variant is measured against the tcgen05 one through this call. */
+int f16acc_gemm_ex(const void *A, int64_t sAm, int64_t sAk,
+                   const void *B, int64_t sBk, int64_t sBn,
+                   void *C, int64_t sCm, int64_t sCn, int c_dtype,
+                   int64_t M, int64_t N, int64_t K, int chunked,
+                   void *workspace, size_t ws_bytes, int device, void *stream,
+                   int variant);
+
+/* The two launches f16acc_gemm_ex makes, one call each (the reference's two
+ * launches, kernel.py:99 `_gemm` and kernel.py:100-104 `_redo`):
+ * f16acc_gemm_main writes C and, when chunked, the per-tile flags into the
+ * workspace; f16acc_gemm_redo, issued later on the same stream with the same
+ * arguments and workspace, recomputes the flagged tiles with FP32
+ * accumulation (a no-op when chunked == 0).  Main followed by redo is exactly
+ * f16acc_gemm_ex; splitting them lets a caller time or schedule each pass. */
+int f16acc_gemm_main(const void *A, int64_t sAm, int64_t sAk,
+                     const void *B, int64_t sBk, int64_t sBn,
+                     void *C, int64_t sCm, int64_t sCn, int c_dtype,
+                     int64_t M, int64_t N, int64_t K, int chunked,
+                     void *workspace, size_t ws_bytes, int device, void *stream,
+                     int variant);
+int f16acc_gemm_redo(const void *A, int64_t sAm, int64_t sAk,
+                     const void *B, int64_t sBk, int64_t sBn,
+                     void *C, int64_t sCm, int64_t sCn, int c_dtype,
+                     int64_t M, int64_t N, int64_t K, int chunked,
+                     void *workspace, size_t ws_bytes, int device, void *stream,
+                     int variant);
+
+/* What f16acc_gemm_ex would run for these operands, without launching:
+ * variant (F16ACC_VARIANT_TCGEN05 or _MMA_SYNC), output tile shape, and the
+ * tile grid (flag slot of tile (tm, tn) = tm * tiles_n + tn, each slot
+ * f16acc_flag_bytes_per_tile() bytes, non-zero bytes = flagged). */
+typedef struct f16acc_plan {
+    int variant;
+    int tile_m, tile_n;
+    int64_t tiles_m, tiles_n;
+} f16acc_plan;
+int f16acc_get_plan(const void *A, int64_t sAm, int64_t sAk,
+                    const void *B, int64_t sBk, int64_t sBn,
+                    int64_t M, int64_t N, int64_t K, int variant, f16acc_plan *out);
+int f16acc_flag_bytes_per_tile(void);
+
+/* Device status word: 0, or the code of the first wait a kernel on `device`
+ * gave up on since the last reset.  Synchronises the device.  reset != 0
+ * clears it.  Returns -1 when the status cannot be read. */
+int f16acc_device_status(int device, int reset);
+
+/* Library build identification (static string). */
+const char *f16acc_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* F16ACC_H_ */

@@ -1,0 +1,60 @@
+"""The C-ABI library loads and exports every symbol include/f16acc.h declares;
+host-only entry points answer without a GPU."""
+
+import os
+import re
+
+import pytest
+
+from f16acc_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "f16acc.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(f16acc_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_gemm_boundary():
+    names = _declared()
+    for n in ("f16acc_gemm", "f16acc_workspace_bytes", "f16acc_strerror"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for n in _declared():
+        assert hasattr(lib, n), n
+    assert set(_declared()) == set(_lib.SIGNATURES)
+
+
+def test_workspace_and_messages():
+    lib = _lib.load()
+    fb = lib.f16acc_flag_bytes_per_tile()
+    assert fb == 16
+    assert lib.f16acc_workspace_bytes(4096, 4096, 4096) == 32 * 32 * fb
+    assert lib.f16acc_workspace_bytes(1, 1, 1) == fb
+    assert lib.f16acc_workspace_bytes(129, 257, 7) == 2 * 3 * fb
+    for code in range(6):
+        assert lib.f16acc_strerror(code)
+    assert b"unknown" in lib.f16acc_strerror(99)
+    assert b"sm_100a" in lib.f16acc_version()
+
+
+def test_invalid_arguments_rejected_before_any_cuda_call():
+    lib = _lib.load()
+    # negative sizes and unknown output codes fail with INVALID_ARGUMENT, no device touched
+    assert lib.f16acc_gemm(None, 0, 0, None, 0, 0, None, 0, 0, 0, -1, 1, 1, 1, None, 0, 0, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.f16acc_gemm(None, 0, 0, None, 0, 0, None, 0, 0, 7, 1, 1, 1, 1, None, 0, 0, None) == _lib.ERR_INVALID_ARGUMENT
+    # empty products are a no-op
+    assert lib.f16acc_gemm(None, 0, 0, None, 0, 0, None, 0, 0, 0, 0, 5, 5, 1, None, 0, 0, None) == _lib.OK
+    assert lib.f16acc_gemm(None, 0, 0, None, 0, 0, None, 0, 0, 0, 5, 0, 5, 1, None, 0, 0, None) == _lib.OK
+
+
+def test_plan_without_a_gpu_is_mma_sync_or_tcgen05():
+    p = _lib.Plan()
+    rc = _lib.load().f16acc_get_plan(16, 64, 1, 16, 1, 64, 128, 128, 64, _lib.VARIANT_MMA_SYNC, p)
+    assert rc == _lib.OK and p.variant == _lib.VARIANT_MMA_SYNC and (p.tile_m, p.tile_n) == (128, 128)
+    assert (p.tiles_m, p.tiles_n) == (1, 1)
