@@ -27,7 +27,6 @@ import json
 import os
 import statistics
 import sys
-import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -55,60 +54,6 @@ def make_inputs(torch, device, seed, sets):
         b = (torch.randn(K, N, device=device, generator=g) * scale).half()
         out.append((a, b))
     return out
-
-
-# ---------------------------------------------------------------- clocks (NVML)
-class ClockSampler:
-    """Samples SM clock and clock-event reasons through NVML while running."""
-
-    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
-               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting",
-               0x1: "gpu_idle"}
-
-    def __init__(self, index: int, period_s: float = 0.01):
-        self.samples, self.reasons, self.max_mhz, self.ok = [], set(), None, False
-        self.period = period_s
-        self._stop = threading.Event()
-        try:
-            import pynvml
-
-            pynvml.nvmlInit()
-            self.nv = pynvml
-            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
-            self.ok = True
-        except Exception as e:  # NVML missing: report, never guess
-            self.err = repr(e)
-
-    def _run(self):
-        nv = self.nv
-        while not self._stop.is_set():
-            try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
-                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                for bit, name in self.REASONS.items():
-                    if mask & bit and name != "gpu_idle":
-                        self.reasons.add(name)
-            except Exception:
-                pass
-            time.sleep(self.period)
-
-    def __enter__(self):
-        if self.ok:
-            self._t = threading.Thread(target=self._run, daemon=True)
-            self._t.start()
-        return self
-
-    def __exit__(self, *exc):
-        if self.ok:
-            self._stop.set()
-            self._t.join()
-
-    def summary(self):
-        if not self.ok:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "err", "nvml")}
-        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
 def measured_peak():
@@ -235,6 +180,7 @@ def run_ours(args):
 
     from f16acc_b200 import _lib
     from f16acc_b200.kernel import mm, mm_phase, plan, tile_flags, workspace_bytes
+    from f16acc_b200.nvml import ClockSampler
 
     world, rank, local = dist_setup(torch, want_nccl=True)
     if args.gpus != world and world > 1:

@@ -11,6 +11,7 @@
 
 #include <cstdint>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "../../include/f16acc.h"
@@ -112,7 +113,11 @@ Layout analyse(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t s
     return L;
 }
 
-constexpr TcShape kTcShape{128, 2};
+// tcgen05 tile configuration: output columns per tile and epilogue column
+// slices per TMEM lane quarter.  Process-wide; f16acc_set_tc_config changes
+// it (tuning and measurement), calls already issued keep theirs.
+std::atomic<int> g_tc_bn{128}, g_tc_epi{2};
+TcShape tc_shape() { return TcShape{g_tc_bn.load(std::memory_order_relaxed), g_tc_epi.load(std::memory_order_relaxed)}; }
 constexpr int kGroupM = 8;
 
 int choose_variant(const Layout& L, int64_t M, int64_t N, int64_t K, int requested) {
@@ -181,8 +186,9 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
     TcParams p;
     std::memset(&p, 0, sizeof(p));
     const bool b_mn = !L.b_tma_k;
+    const TcShape shape = tc_shape();
     if (v == F16ACC_VARIANT_TCGEN05) {
-        const int bn = kTcShape.bn;
+        const int bn = shape.bn;
         const bool maps_ok =
             make_map(&p.tmA, A, uint64_t(K), uint64_t(M), uint64_t(L.sAm) * 2, 64, 128) &&
             (b_mn ? make_map(&p.tmB, B, uint64_t(N), uint64_t(K), uint64_t(L.sBk) * 2, 64, 64)
@@ -193,7 +199,7 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
         }
     }
     if (v == F16ACC_VARIANT_TCGEN05) {
-        const int bn = kTcShape.bn;
+        const int bn = shape.bn;
         p.C = C;
         p.sCm = sCm;
         p.sCn = sCn;
@@ -209,10 +215,10 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
         const int64_t tiles = int64_t(p.tiles_m) * p.tiles_n;
         const int grid = int(tiles < info->sms ? tiles : info->sms);
         if ((phases & kPhaseMain) &&
-            launch_tc(p, kTcShape, chunked != 0, b_mn, c_dtype, false, grid, stream) != cudaSuccess)
+            launch_tc(p, shape, chunked != 0, b_mn, c_dtype, false, grid, stream) != cudaSuccess)
             return F16ACC_ERR_CUDA;
         if (chunked && (phases & kPhaseRedo) &&
-            launch_tc(p, kTcShape, false, b_mn, c_dtype, true, grid, stream) != cudaSuccess)
+            launch_tc(p, shape, false, b_mn, c_dtype, true, grid, stream) != cudaSuccess)
             return F16ACC_ERR_CUDA;
         return F16ACC_OK;
     }
@@ -315,13 +321,33 @@ int f16acc_get_plan(const void* A, int64_t sAm, int64_t sAk, const void* B, int6
     if (v < 0) return variant == F16ACC_VARIANT_AUTO ? F16ACC_ERR_INVALID_ARGUMENT : F16ACC_ERR_UNSUPPORTED;
     out->variant = v;
     out->tile_m = 128;
-    out->tile_n = v == F16ACC_VARIANT_TCGEN05 ? kTcShape.bn : MmaCfg::BN;
+    out->tile_n = v == F16ACC_VARIANT_TCGEN05 ? tc_shape().bn : MmaCfg::BN;
     out->tiles_m = cdiv(M, out->tile_m);
     out->tiles_n = cdiv(N, out->tile_n);
     return F16ACC_OK;
 }
 
 int f16acc_flag_bytes_per_tile(void) { return kFlagBytesPerTile; }
+
+int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void* out, int device, void* stream) {
+    if (mode < 0 || mode > 2 || chunks < 0 || grid <= 0 || out == nullptr) return F16ACC_ERR_INVALID_ARGUMENT;
+    if (mode == 2 && epi_split != 2 && epi_split != 4) return F16ACC_ERR_INVALID_ARGUMENT;
+    DeviceInfo* info = device_info(device);
+    if (!info) return F16ACC_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess || info->err != cudaSuccess) return F16ACC_ERR_CUDA;
+    return launch_chunk_rate(mode, epi_split, chunks, grid, static_cast<float*>(out), info->status,
+                             static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? F16ACC_OK
+               : F16ACC_ERR_CUDA;
+}
+
+int f16acc_set_tc_config(int tile_n, int epi_split) {
+    if (!tc_shape_supported(TcShape{tile_n, epi_split})) return F16ACC_ERR_INVALID_ARGUMENT;
+    g_tc_bn.store(tile_n);
+    g_tc_epi.store(epi_split);
+    return F16ACC_OK;
+}
 
 int f16acc_device_status(int device, int reset) {
     DeviceInfo* info = device_info(device);

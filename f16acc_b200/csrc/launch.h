@@ -30,6 +30,11 @@ cudaError_t launch_mma(const MmaParams& p, bool chunked, int a_mode, int b_mode,
                        cudaStream_t stream);
 cudaError_t launch_fill_zero(void* C, int64_t sCm, int64_t sCn, int M, int N, int out, cudaStream_t stream);
 
+// Raw-rate probe (probes.cu): mode 0/1 MMA only with FP16/FP32 accumulator,
+// mode 2 the chunk pipeline; `out` holds grid * (64 + 128 * epi_split) floats.
+cudaError_t launch_chunk_rate(int mode, int epi_split, int chunks, int grid, float* out, int* status,
+                              cudaStream_t stream);
+
 // Launch helper: cudaLaunchKernelEx with optional programmatic stream
 // serialisation (the dependent kernel may start its prologue while the
 // previous kernel on the stream drains; it calls griddepcontrol.wait before

@@ -30,6 +30,7 @@
 
 #include "common.cuh"
 #include "ptx.cuh"
+#include "tc_epilogue.cuh"
 
 namespace f16acc {
 
@@ -64,7 +65,10 @@ struct TcConfig {
     static constexpr int NBUF = TMEM_COLS / ACC_COLS;
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*alignment slack*/ + BAR_BYTES;
-    static_assert(EPI_WARPS * 2 <= kFlagBytesPerTile, "flag slot holds two bytes per epilogue warp");
+    static constexpr int FLAG_BYTES_PER_WARP = kFlagBytesPerTile / EPI_WARPS;  // every slot byte gets written
+    static_assert(FLAG_BYTES_PER_WARP * EPI_WARPS == kFlagBytesPerTile &&
+                      (FLAG_BYTES_PER_WARP == 1 || FLAG_BYTES_PER_WARP == 2),
+                  "flag slot split over the epilogue warps");
     static_assert(CW == 32 || CW % 64 == 0, "epilogue column slice");
     static_assert((2 * STAGES + 2 * NBUF + 1) * 8 + 16 <= BAR_BYTES, "barrier area");
 };
@@ -228,69 +232,40 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT>::THREADS, 1)
         const int q = warp & 3;          // TMEM lane quarter this warp may access
         const int colg = e >> 2;         // column slice
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-        uint32_t b = 0, tph = 0;
+        ChunkRing<NBUF> ring{tfull, tempty, tmem + lane_base + colg * CW, Cfg::ACC_COLS};
         for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
             int tm, tn;
             raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
             const int64_t tile_id = static_cast<int64_t>(tm) * p.tiles_n + tn;
             if (REDO && !tile_flagged(p.flags, tile_id)) continue;
             float acc[CW];
-            bool ok = true;
             if constexpr (CHUNKED) {
 #pragma unroll
                 for (int j = 0; j < CW; ++j) acc[j] = 0.0f;
-                for (int c = 0; c < nchunks; ++c) {
-                    ok = mbar_wait(&tfull[b], tph, abort_flag, p.status, kStatusTimeoutEpilogue);
-                    if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-                    tc_fence_after();
-                    const uint32_t taddr = tmem + lane_base + b * Cfg::ACC_COLS + colg * CW;
-                    if constexpr (CW == 32) {
-                        uint32_t r[16];
-                        tmem_ld_32x32b_x16_pack16(taddr, r);
-                        tmem_wait_ld();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&tempty[b]);
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) add_f16x2_to_f32(acc[2 * i], acc[2 * i + 1], r[i]);
-                    } else {
-                        uint32_t r[CW / 2];
-#pragma unroll
-                        for (int j = 0; j < CW / 64; ++j)
-                            tmem_ld_32x32b_x32_pack16(taddr + j * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[j * 32]));
-                        tmem_wait_ld();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&tempty[b]);
-#pragma unroll
-                        for (int i = 0; i < CW / 2; ++i) add_f16x2_to_f32(acc[2 * i], acc[2 * i + 1], r[i]);
-                    }
-                    if (++b == NBUF) { b = 0; tph ^= 1u; }
-                }
-                if (!ok) break;
+                if (!consume_chunks<CW, NBUF>(acc, nchunks, ring, lane, abort_flag, p.status)) break;
                 float z = 0.0f;
 #pragma unroll
                 for (int j = 0; j < CW; ++j) z = nonfinite_probe(z, acc[j]);
                 const bool bad = __any_sync(0xffffffffu, z != z);
-                if (lane == 0)
-                    *reinterpret_cast<uint16_t*>(p.flags + tile_id * kFlagBytesPerTile + 2 * e) = bad ? 1 : 0;
+                if (lane == 0) {
+                    uint8_t* slot = p.flags + tile_id * kFlagBytesPerTile;
+                    if constexpr (Cfg::FLAG_BYTES_PER_WARP == 2)
+                        *reinterpret_cast<uint16_t*>(slot + 2 * e) = bad ? 1 : 0;
+                    else
+                        slot[e] = bad ? 1 : 0;
+                }
             } else {
-                ok = mbar_wait(&tfull[b], tph, abort_flag, p.status, kStatusTimeoutEpilogue);
-                if (!__all_sync(0xffffffffu, ok)) break;
-                tc_fence_after();
-                const uint32_t taddr = tmem + lane_base + b * Cfg::ACC_COLS + colg * CW;
+                if (!ring.wait_full(abort_flag, p.status)) break;
 #pragma unroll
                 for (int j = 0; j < CW / 32; ++j) {
                     uint32_t r[32];
-                    tmem_ld_32x32b_x32(taddr + j * 32, r);
+                    tmem_ld_32x32b_x32(ring.addr() + j * 32, r);
                     tmem_wait_ld();
+                    reg_fence(r);
 #pragma unroll
                     for (int i = 0; i < 32; ++i) acc[j * 32 + i] = __uint_as_float(r[i]);
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[b]);
-                if (++b == NBUF) { b = 0; tph ^= 1u; }
+                ring.release(lane);
             }
             const int row = tm * BM + q * 32 + lane;
             const int col0 = tn * BN + colg * CW;

@@ -63,16 +63,26 @@ cudaError_t launch_shape(const TcParams& p, bool chunked, bool b_mn, int out, bo
 
 }  // namespace
 
-bool tc_shape_supported(TcShape s) { return s.bn == 128 && s.epi_split == 2; }
+bool tc_shape_supported(TcShape s) { return s.bn == 128 && (s.epi_split == 2 || s.epi_split == 4); }
 
-int tc_threads(TcShape s) { return s.bn == 128 && s.epi_split == 2 ? TcConfig<128, 2>::THREADS : 0; }
+int tc_threads(TcShape s) {
+    if (s.bn == 128 && s.epi_split == 2) return TcConfig<128, 2>::THREADS;
+    if (s.bn == 128 && s.epi_split == 4) return TcConfig<128, 4>::THREADS;
+    return 0;
+}
 
-int tc_smem_bytes(TcShape s) { return s.bn == 128 && s.epi_split == 2 ? TcConfig<128, 2>::SMEM_BYTES : 0; }
+int tc_smem_bytes(TcShape s) {
+    if (s.bn == 128 && s.epi_split == 2) return TcConfig<128, 2>::SMEM_BYTES;
+    if (s.bn == 128 && s.epi_split == 4) return TcConfig<128, 4>::SMEM_BYTES;
+    return 0;
+}
 
 cudaError_t launch_tc(const TcParams& p, TcShape shape, bool chunked, bool b_mn, int out, bool redo, int grid,
                       cudaStream_t stream) {
     if (shape.bn == 128 && shape.epi_split == 2)
         return launch_shape<128, 2>(p, chunked, b_mn, out, redo, grid, stream);
+    if (shape.bn == 128 && shape.epi_split == 4)
+        return launch_shape<128, 4>(p, chunked, b_mn, out, redo, grid, stream);
     return cudaErrorInvalidValue;
 }
 

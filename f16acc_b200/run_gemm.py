@@ -32,7 +32,10 @@ def main(argv=None) -> int:
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--check", action="store_true", help="max rel err vs an FP64 product")
+    ap.add_argument("--epi", type=int, default=None, help="tcgen05 epilogue column slices per lane quarter (2 or 4)")
     a = ap.parse_args(argv)
+    if a.epi is not None and _lib.load().f16acc_set_tc_config(128, a.epi) != 0:
+        raise SystemExit(f"unsupported --epi {a.epi}")
 
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev).manual_seed(a.seed)

@@ -123,6 +123,21 @@ int f16acc_get_plan(const void *A, int64_t sAm, int64_t sAk,
                     int64_t M, int64_t N, int64_t K, int variant, f16acc_plan *out);
 int f16acc_flag_bytes_per_tile(void);
 
+/* tcgen05 tile configuration for later calls, process-wide: output columns
+ * per tile (128) and epilogue column slices per TMEM lane quarter (2 or 4,
+ * i.e. 8 or 16 epilogue warps).  A tuning knob; do not change it between an
+ * f16acc_gemm_main and its f16acc_gemm_redo. */
+int f16acc_set_tc_config(int tile_n, int epi_split);
+
+/* Raw-rate probe, the B200 counterpart of the reference's bench/rate.py and
+ * bench/chunkrate.py: `grid` CTAs (one per SM) each run `chunks` 32-long
+ * chunks of 128x128 tcgen05 MMAs on a fixed shared-memory tile.  mode 0: MMA
+ * only, FP16 accumulator; mode 1: MMA only, FP32 accumulator; mode 2: the
+ * GEMM kernel's chunk pipeline (MMA + TMEM load + FP32 add per element) with
+ * epi_split 2 or 4.  `out` is device memory for grid * (64 + 128*epi_split)
+ * floats.  Asynchronous on `stream`; time it with events. */
+int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void *out, int device, void *stream);
+
 /* Device status word: 0, or the code of the first wait a kernel on `device`
  * gave up on since the last reset.  Synchronises the device.  reset != 0
  * clears it.  Returns -1 when the status cannot be read. */

@@ -20,17 +20,20 @@ def ulp16(x):
 
 def chunk_ulp_bound(a16, b16, ulps=2.0, chunk=32):
     """Per-element bound on |x - y| for two chunked products that may round
-    each FP16 chunk sum differently (summation order inside a chunk is
-    hardware defined): `ulps` FP16 ulps of every chunk value, plus FP32
-    rounding of the running sums."""
+    each FP16 chunk sum differently (where and how often the FP16 accumulator
+    rounds inside a chunk is hardware defined): `ulps` FP16 ulps at the
+    magnitude of the chunk's absolute sum (an upper bound on every partial sum
+    inside the chunk, so cancellation is covered), plus FP32 rounding of the
+    running sums."""
     a = np.asarray(a16, dtype=np.float64)
     b = np.asarray(b16, dtype=np.float64)
     K = a.shape[1]
     bound = np.zeros((a.shape[0], b.shape[1]))
     run = np.zeros_like(bound)
+    aa, ab = np.abs(a), np.abs(b)
     for k0 in range(0, K, chunk):
-        part = a[:, k0:k0 + chunk] @ b[k0:k0 + chunk]
-        run += np.abs(part)
-        bound += ulps * ulp16(part)
+        absum = aa[:, k0:k0 + chunk] @ ab[k0:k0 + chunk]
+        run += absum
+        bound += ulps * ulp16(absum)
     nch = max(1, (K + chunk - 1) // chunk)
     return bound + nch * run * 2.0 ** -23 + 1e-30

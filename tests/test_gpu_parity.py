@@ -6,7 +6,8 @@ defined (the reference leaves it to Triton), so two correct chunked results
 may differ by a rounding of each chunk sum: the bound is 2 FP16 ulps of every
 chunk value plus FP32 rounding of the running sum (tests/helpers.py).  Tile
 flags, the overflow known answer, and redone tiles against the kernel's own
-FP32-accumulate output are exact.  FP32-accumulate results: 2^-20 of max|ref|.
+FP32-accumulate output are exact.  FP32-accumulate results (hardware order
+of FP32 additions): F32_TOL = 1e-5 of max|ref|.
 """
 
 import os
@@ -26,6 +27,7 @@ pytestmark = pytest.mark.gpu
 VARIANTS = [_lib.VARIANT_TCGEN05, _lib.VARIANT_MMA_SYNC]
 VNAMES = {_lib.VARIANT_TCGEN05: "tcgen05", _lib.VARIANT_MMA_SYNC: "mma_sync"}
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "reference_cases.npz")
+F32_TOL = 1e-5
 
 
 def padded(x: torch.Tensor, mult: int = 8) -> torch.Tensor:
@@ -90,7 +92,7 @@ def test_golden_reference_outputs(cuda, variant, name, d):
         assert (cc == 100.0).all()
         return
     if not chunked:
-        assert np.abs(cc - ref).max() <= np.abs(ref).max() * 2.0 ** -20
+        assert np.abs(cc - ref).max() <= np.abs(ref).max() * F32_TOL
         return
     bound = chunk_ulp_bound(d["a"], np16(b), ulps=2.0)
     if out_dtype == torch.float16:
@@ -104,7 +106,7 @@ def test_golden_reference_outputs(cuda, variant, name, d):
     either = redone | ours_redone
     f32 = O.gemm_f32acc(d["a"], np16(b)).astype(np.float64)
     # where exactly one side redid a tile, values are compared to the FP32 product instead
-    both_ok = np.where(either, np.abs(cc - f32) <= np.abs(f32) * 2.0 ** -20 + 1e-30, np.abs(cc - ref) <= bound)
+    both_ok = np.where(either, np.abs(cc - f32) <= np.abs(f32).max() * F32_TOL, np.abs(cc - ref) <= bound)
     assert both_ok.all(), float(np.abs(cc - ref).max())
 
 
@@ -195,7 +197,7 @@ def test_fp32_accumulate_mode(cuda, variant):
     b = torch.randn(500, 260, generator=g).half().to(cuda)
     c, *_ = run(a, b, variant, chunked=False)
     ref = O.gemm_f64(np16(a), np16(b))
-    assert np.abs(c.double().cpu().numpy() - ref).max() <= np.abs(ref).max() * 2.0 ** -20
+    assert np.abs(c.double().cpu().numpy() - ref).max() <= np.abs(ref).max() * F32_TOL
 
 
 def test_empty_shapes(cuda):
@@ -307,21 +309,24 @@ def test_config2_4096_accuracy(cuda, layout, out_dtype):
     assert r2 <= 1e-3
 
 
-def test_config4_overflow_stress_4096(cuda):
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32], ids=str)
+def test_config4_overflow_stress_4096(cuda, out_dtype):
     # N(0,1) seed 3, 1% of A rows and B cols x64
     a, b = stress(4096, 4096, 4096, seed=3, scale=64.0)
     a, b = a.to(cuda), b.to(cuda)
-    c, ws = mm_ex(a, b, torch.float16)
-    c32, _ = mm_ex(a, b, torch.float16, chunked=False)
+    c, ws = mm_ex(a, b, out_dtype)
+    c32, _ = mm_ex(a, b, out_dtype, chunked=False)
     pl = plan(a, b)
     flags = tile_flags(ws, pl)
     assert flags.any()
     tm, tn = pl["tile"]
     mask = flags.repeat_interleave(tm, 0).repeat_interleave(tn, 1)[: c.shape[0], : c.shape[1]]
-    assert torch.equal(c[mask], c32[mask])
-    assert torch.isfinite(c).all()
+    assert torch.equal(c[mask], c32[mask])  # redone tiles == the FP32-accumulate path, bit for bit
     ref = a.double() @ b.double()
-    assert ((c.double() - ref).abs().max() / ref.abs().max()).item() < 1e-3
+    # an fp16 store of |C| > 65504 is inf, exactly as the reference's cast (kernel.py:59); never NaN
+    fits = ref.abs() < 65000 if out_dtype == torch.float16 else torch.ones_like(ref, dtype=torch.bool)
+    assert torch.isfinite(c[fits]).all() and not torch.isnan(c).any()
+    assert ((c.double()[fits] - ref[fits]).abs().max() / ref.abs().max()).item() < 1e-3
 
 
 def test_device_status_clean(cuda):
