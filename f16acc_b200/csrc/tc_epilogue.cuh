@@ -41,7 +41,10 @@ __device__ __forceinline__ void add_chunk(float (&acc)[CW], const uint32_t (&r)[
 // Ring of NBUF chunk accumulators in TMEM shared with the MMA warp:
 // tfull[b] completes when chunk b's MMAs are done, tempty[b] gets one arrival
 // per epilogue warp once that warp has its values in registers.
-template <int NBUF>
+// PER_THREAD: every thread arrives on tempty (barrier count = 32 x epilogue
+// warps) instead of one elected lane after a __syncwarp.  NO_FENCE drops the
+// tcgen05 fences (only valid where no tcgen05 op is ordered by the hand-off).
+template <int NBUF, bool SPIN = false, bool PER_THREAD = false, bool NO_FENCE = false>
 struct ChunkRing {
     uint64_t* tfull;
     uint64_t* tempty;
@@ -51,23 +54,28 @@ struct ChunkRing {
 
     __device__ __forceinline__ uint32_t addr() const { return col_base + b * stride; }
     __device__ __forceinline__ bool wait_full(volatile int* abort, int* status) {
-        const bool ok = mbar_wait(&tfull[b], phase, abort, status, kStatusTimeoutEpilogue);
+        const bool ok = SPIN ? mbar_wait_spin(&tfull[b], phase, abort, status, kStatusTimeoutEpilogue)
+                             : mbar_wait(&tfull[b], phase, abort, status, kStatusTimeoutEpilogue);
         if (!__all_sync(0xffffffffu, ok)) return false;
-        tc_fence_after();
+        if (!NO_FENCE) tc_fence_after();
         return true;
     }
     __device__ __forceinline__ void release(int lane) {
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[b]);
+        if (!NO_FENCE) tc_fence_before();
+        if (PER_THREAD) {
+            mbar_arrive(&tempty[b]);
+        } else {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);
+        }
         if (++b == NBUF) { b = 0; phase ^= 1u; }
     }
 };
 
 // Sum `nchunks` chunk accumulators into acc (FP32), consuming them from the
 // ring in order.  Returns false when a wait gave up (nothing in flight then).
-template <int CW, int NBUF>
-__device__ __forceinline__ bool consume_chunks(float (&acc)[CW], int nchunks, ChunkRing<NBUF>& ring, int lane,
+template <int CW, typename Ring>
+__device__ __forceinline__ bool consume_chunks(float (&acc)[CW], int nchunks, Ring& ring, int lane,
                                                volatile int* abort, int* status) {
     uint32_t ra[CW / 2], rb[CW / 2];
     if (nchunks <= 0) return true;

@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT>::THREADS, 1)
             if constexpr (CHUNKED) {
 #pragma unroll
                 for (int j = 0; j < CW; ++j) acc[j] = 0.0f;
-                if (!consume_chunks<CW, NBUF>(acc, nchunks, ring, lane, abort_flag, p.status)) break;
+                if (!consume_chunks<CW>(acc, nchunks, ring, lane, abort_flag, p.status)) break;
                 float z = 0.0f;
 #pragma unroll
                 for (int j = 0; j < CW; ++j) z = nonfinite_probe(z, acc[j]);

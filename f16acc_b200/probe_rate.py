@@ -59,13 +59,61 @@ def main(argv=None) -> int:
     a = ap.parse_args(argv)
     dev = torch.device("cuda:0")
     probes = [("mma_f16acc", 0, 2), ("mma_f32acc", 1, 2), ("chunk_pipeline_8warp", 2, 2),
-              ("chunk_pipeline_16warp", 2, 4)]
+              ("chunk_pipeline_16warp", 2, 4), ("pipeline_no_adds_8warp", 3, 2), ("pipeline_no_adds_16warp", 3, 4),
+              ("handoff_only_8warp", 4, 2), ("tmem_ld_only_8warp", 6, 2), ("tmem_ld_only_16warp", 6, 4),
+              ("tmem_ld_add_8warp", 7, 2), ("tmem_ld_add_16warp", 7, 4),
+              ("chunk_pipeline_8warp_spin", 12, 2), ("handoff_only_8warp_spin", 13, 2),
+              ("pingpong_no_mma_8warp", 14, 2), ("pingpong_no_mma_8warp_spin", 15, 2),
+              ("pingpong_no_mma_8slots", 20, 2), ("mma_f16acc_n64", 21, 2), ("mma_f16acc_n256", 22, 2),
+              ("chunk_pipeline_merged_issuer", 23, 2), ("pingpong_no_fence", 24, 2),
+              ("pingpong_per_thread_arrive", 25, 2), ("pingpong_no_fence_per_thread", 26, 2),
+              ("handoff_per_thread_arrive", 27, 2), ("mma_issue_commit_only", 28, 2)]
     for name, mode, epi in probes:
         sms, ms, tflops, clk = run(mode, epi, a.chunks, a.reps, dev)
         mhz = clk.get("sm_mhz")
         peak = sms * 8192 * mhz * 1e6 / 1e12 if mhz else None
         print(json.dumps({"probe": name, "chunks_per_cta": a.chunks, "ms": ms, "tflops": tflops, "clocks": clk,
                           "frac_of_clock_peak": tflops / peak if peak else None}), flush=True)
+    # warp-level mma.sync: 4 blocks of 8 warps per SM, 8 independent chains per warp
+    for name, mode in (("mma_sync_f16acc", 30), ("mma_sync_f32acc", 31), ("mma_sync_chunk32", 32)):
+        lib = _lib.load()
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        grid = 4 * sms
+        out = torch.empty(grid * 256, device=dev)
+        iters = max(1024, a.chunks // 4)
+        stream = torch.cuda.current_stream(dev)
+
+        def launch():
+            rc = lib.f16acc_probe_chunk_rate(mode, 2, iters, grid, out.data_ptr(), dev.index or 0, stream.cuda_stream)
+            if rc != 0:
+                raise RuntimeError(_lib.strerror(rc))
+
+        launch()
+        torch.cuda.synchronize()
+        with ClockSampler(dev.index or 0, period_s=0.002) as clocks:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(a.reps):
+                launch()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / a.reps
+        steps = 2 if mode == 32 else 1
+        tflops = grid * 8 * iters * steps * 8 * 4096 / (ms / 1e3) / 1e12
+        clk = clocks.summary()
+        mhz = clk.get("sm_mhz")
+        peak = sms * 8192 * mhz * 1e6 / 1e12 if mhz else None
+        print(json.dumps({"probe": name, "iters": iters, "ms": ms, "tflops": tflops, "clocks": clk,
+                          "frac_of_clock_peak": tflops / peak if peak else None}), flush=True)
+    # latency: one thread, a dependent MMA group + commit + mbarrier wait per iteration
+    lat = [("latency_2mma_n128", 8), ("latency_1mma_n128", 9), ("latency_2mma_n64", 10), ("latency_8mma_n128", 11)]
+    iters = max(256, a.chunks // 16)
+    for name, mode in lat:
+        sms, ms, _, clk = run(mode, 2, iters, a.reps, dev)
+        ns = ms * 1e6 / iters
+        mhz = clk.get("sm_mhz") or 0
+        print(json.dumps({"probe": name, "iters": iters, "ns_per_group": ns,
+                          "cycles_per_group": ns * mhz / 1e3 if mhz else None, "clocks": clk}), flush=True)
     st = _lib.load().f16acc_device_status(dev.index or 0, 1)
     if st != 0:
         print(json.dumps({"device_status": st}))

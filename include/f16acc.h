@@ -134,8 +134,22 @@ int f16acc_set_tc_config(int tile_n, int epi_split);
  * chunks of 128x128 tcgen05 MMAs on a fixed shared-memory tile.  mode 0: MMA
  * only, FP16 accumulator; mode 1: MMA only, FP32 accumulator; mode 2: the
  * GEMM kernel's chunk pipeline (MMA + TMEM load + FP32 add per element) with
- * epi_split 2 or 4.  `out` is device memory for grid * (64 + 128*epi_split)
- * floats.  Asynchronous on `stream`; time it with events. */
+ * epi_split 2 or 4.  Breakdown modes: 3 = mode 2 without the adds, 4 = the
+ * MMA/epilogue hand-off alone (no TMEM loads), 6 = TMEM loads alone (no MMA,
+ * no hand-off), 7 = TMEM loads + adds (no MMA).  Latency modes (one thread:
+ * an MMA group, commit, wait): 8 = 2 MMAs N=128, 9 = 1 MMA N=128, 10 = 2 MMAs
+ * N=64, 11 = 8 MMAs N=128.  Spinning-wait variants: 12 = mode 2, 13 = mode 4,
+ * 15 = barrier ping-pong without MMAs (14 = the same with suspending waits),
+ * 20 = the ping-pong with 8 slots.  21 / 22 = MMA only with N=64 / N=256
+ * instructions; 23 = chunk pipeline whose epilogue warps issue the next
+ * chunk's MMAs themselves after a named barrier.  24 / 25 / 26 = ping-pong
+ * without tcgen05 fences / with per-thread arrives / both; 27 = mode 4 with
+ * per-thread arrives; 28 = MMA issue with a commit per chunk, no waiting.
+ * Warp-level mma.sync rate (grid blocks of 8
+ * warps, 8 m16n8k16 chains per warp, `chunks` iterations): 30 = FP16
+ * accumulate, 31 = FP32 accumulate, 32 = FP16 chunks of 2 steps added into FP32.
+ * `out` is device memory for grid * max(256, 64 + 128*epi_split) floats.
+ * Asynchronous on `stream`; time it with events. */
 int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void *out, int device, void *stream);
 
 /* Device status word: 0, or the code of the first wait a kernel on `device`
