@@ -182,7 +182,8 @@ def test_strided_outputs_through_the_c_abi(cuda):
         wide = torch.full((200, 300), -7.0, device=cuda)
         out = wide[:, 50:210]
         mm_ex(a, b, torch.float32, variant=variant, out=out)
-        assert torch.equal(out, ref) or variant != _lib.VARIANT_AUTO
+        if variant == plan(a, b)["variant"]:
+            assert torch.equal(out, ref)  # same kernel as the contiguous-output call
         assert (wide[:, :50] == -7).all() and (wide[:, 210:] == -7).all()
         check_chunked(out, a, b)
         colmajor = torch.empty(160, 200, device=cuda).t()
@@ -331,3 +332,29 @@ def test_config4_overflow_stress_4096(cuda, out_dtype):
 
 def test_device_status_clean(cuda):
     assert device_status(0, reset=True) == 0
+
+
+# ---------------------------------------------------------------- hardware rounding inside a chunk
+
+@pytest.mark.parametrize("dist", ["normal", "uniform", "wide"])
+def test_chunk_rounding_matches_round_every_16(cuda, dist):
+    """K = 32, so C is one chunk value converted exactly to FP32.  Both
+    variants give bit-identical chunk values, and they equal the oracle's
+    round-after-each-K=16 emulation in (almost) every element."""
+    g = torch.Generator().manual_seed(1)
+    if dist == "normal":
+        a, b = torch.randn(512, 32, generator=g), torch.randn(32, 512, generator=g)
+    elif dist == "uniform":
+        a, b = torch.rand(512, 32, generator=g) * 2 - 1, torch.rand(32, 512, generator=g) * 2 - 1
+    else:
+        a = torch.randn(512, 32, generator=g) * torch.exp2(torch.randint(-6, 6, (512, 32), generator=g).float())
+        b = torch.randn(32, 512, generator=g)
+    a, b = a.half(), b.half()
+    r16, _ = O.gemm_chunked(a.numpy(), b.numpy(), round_every=16)
+    r32, _ = O.gemm_chunked(a.numpy(), b.numpy(), round_every=32)
+    outs = [mm_ex(a.to(cuda), b.to(cuda), torch.float32, variant=v)[0].cpu().numpy() for v in VARIANTS]
+    assert np.array_equal(outs[0], outs[1])
+    eq16 = float((outs[0] == r16).mean())
+    eq32 = float((outs[0] == r32).mean())
+    print(f"\n{dist}: equal to round_every=16 {eq16:.5f}, to round_every=32 {eq32:.5f}")
+    assert eq16 > 0.999 and eq16 > eq32
