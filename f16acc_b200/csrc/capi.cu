@@ -309,6 +309,9 @@ const char* f16acc_strerror(int code) {
         case F16ACC_ERR_UNSUPPORTED: return "the requested kernel variant cannot take these operands";
         case F16ACC_ERR_CUDA: return "a CUDA call or kernel launch failed";
         case F16ACC_ERR_DEVICE_TIMEOUT: return "a kernel gave up waiting on the device (see f16acc_device_status)";
+        case F16ACC_ERR_TOO_LARGE:
+            return "output needs more 128x128 tiles than f16acc_gemm_noalloc's fixed flag array holds "
+                   "(F16ACC_NOALLOC_MAX_TILES); use f16acc_gemm with a workspace";
     }
     return "unknown f16acc error code";
 }

@@ -1,0 +1,77 @@
+// noalloc.cu -- f16acc_gemm_noalloc: the chunked GEMM for callers that cannot
+// allocate device memory.
+//
+// f16acc_gemm needs a caller-provided workspace for its per-tile overflow
+// flags.  Some callers have no way to provide one: a plain C or FFI host
+// program that links only this library and holds raw pointers but no device
+// allocator, or a latency-critical loop that must not call cudaMalloc at all
+// (cudaMalloc can synchronise the whole device and can fail when memory is
+// tight).  This entry point keeps the flags in a fixed array compiled into
+// the library instead, so it allocates nothing.
+//
+// The array lives in device memory on every GPU that loads the library, until
+// the process exits.  All calls on a device share it and it keeps the last
+// call's contents; that is harmless here because the main pass writes every
+// flag byte of every tile it covers before the redo pass reads it, so nothing
+// has to start at zero.  Two calls whose work overlaps on the GPU (different
+// streams, or different host threads) race on the array: serialise them, e.g.
+// issue them on one stream.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+
+#include "../../include/f16acc.h"
+
+namespace f16acc {
+namespace {
+
+// Room for F16ACC_NOALLOC_MAX_TILES output tiles of 128 x 128 at 16 flag
+// bytes each (1 MiB per device).
+constexpr size_t kNoAllocFlagBytes = size_t(F16ACC_NOALLOC_MAX_TILES) * 16;
+
+// The scratch array.  In host code this name is only a host-side stand-in:
+// its device address comes from cudaGetSymbolAddress below, never from
+// taking the address of the symbol on the host.
+static __device__ __align__(256) uint8_t g_noalloc_flags[kNoAllocFlagBytes];
+
+constexpr int kMaxDevices = 64;
+
+struct NoAllocSlot {
+    std::once_flag once;
+    cudaError_t err = cudaSuccess;
+    void* ptr = nullptr;  // device address of g_noalloc_flags on this device
+};
+NoAllocSlot g_slots[kMaxDevices];
+
+// Once per device, with that device current: resolve the array's device address.
+void* scratch_for(int device) {
+    NoAllocSlot& s = g_slots[device];
+    std::call_once(s.once, [&s, device]() {
+        int prev = -1;
+        s.err = cudaGetDevice(&prev);
+        if (s.err != cudaSuccess) return;
+        if (prev != device && (s.err = cudaSetDevice(device)) != cudaSuccess) return;
+        void* p = nullptr;
+        s.err = cudaGetSymbolAddress(&p, g_noalloc_flags);
+        if (s.err == cudaSuccess) s.ptr = p;
+        if (prev != device) cudaSetDevice(prev);
+    });
+    return s.err == cudaSuccess ? s.ptr : nullptr;
+}
+
+}  // namespace
+}  // namespace f16acc
+
+extern "C" int f16acc_gemm_noalloc(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int64_t sBn,
+                                   void* C, int64_t sCm, int64_t sCn, int c_dtype, int64_t M, int64_t N, int64_t K,
+                                   int chunked, int device, void* stream) {
+    if (device < 0 || device >= f16acc::kMaxDevices) return F16ACC_ERR_INVALID_ARGUMENT;
+    if (M < 0 || N < 0 || K < 0) return F16ACC_ERR_INVALID_ARGUMENT;
+    const size_t need = f16acc_workspace_bytes(M, N, K);
+    if (chunked && need > f16acc::kNoAllocFlagBytes) return F16ACC_ERR_TOO_LARGE;
+    void* flags = f16acc::scratch_for(device);
+    if (flags == nullptr) return F16ACC_ERR_CUDA;
+    return f16acc_gemm(A, sAm, sAk, B, sBk, sBn, C, sCm, sCn, c_dtype, M, N, K, chunked, flags,
+                       f16acc::kNoAllocFlagBytes, device, stream);
+}

@@ -39,6 +39,7 @@ extern "C" {
 #define F16ACC_ERR_UNSUPPORTED 3      /* forced variant cannot take these operands */
 #define F16ACC_ERR_CUDA 4             /* a CUDA runtime call or launch failed */
 #define F16ACC_ERR_DEVICE_TIMEOUT 5   /* a kernel gave up on a wait (see f16acc_device_status) */
+#define F16ACC_ERR_TOO_LARGE 6        /* more output tiles than f16acc_gemm_noalloc's fixed flag array holds */
 
 /* Output element types (c_dtype); kernel.py:93 allocates C as out_dtype. */
 #define F16ACC_OUT_F16 0
@@ -156,6 +157,27 @@ int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void 
  * gave up on since the last reset.  Synchronises the device.  reset != 0
  * clears it.  Returns -1 when the status cannot be read. */
 int f16acc_device_status(int device, int reset);
+
+/* f16acc_gemm for callers that cannot allocate device memory.  No counterpart
+ * in the reference.  Same arguments as f16acc_gemm minus the workspace: the
+ * per-tile overflow flags go to a fixed array compiled into the library
+ * (F16ACC_NOALLOC_MAX_TILES tiles of 128 x 128, 1 MiB on every GPU that loads
+ * the library, held until the process exits), so the call allocates nothing.
+ * For callers that have no device allocator (a plain C or FFI host program
+ * holding raw pointers) or must not call cudaMalloc on this path (it can
+ * synchronise the device and can fail under memory pressure).
+ * Limit: a chunked call whose output needs more than F16ACC_NOALLOC_MAX_TILES
+ * tiles (e.g. beyond 32768 x 32768) returns F16ACC_ERR_TOO_LARGE without
+ * launching.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) and must come before any stream capture on that
+ * device.  All calls share the array: calls whose work overlaps on the GPU
+ * (other streams, other host threads) race and must be serialised. */
+#define F16ACC_NOALLOC_MAX_TILES 65536
+int f16acc_gemm_noalloc(const void *A, int64_t sAm, int64_t sAk,
+                        const void *B, int64_t sBk, int64_t sBn,
+                        void *C, int64_t sCm, int64_t sCn, int c_dtype,
+                        int64_t M, int64_t N, int64_t K, int chunked,
+                        int device, void *stream);
 
 /* Library build identification (static string). */
 const char *f16acc_version(void);
