@@ -333,7 +333,8 @@ int f16acc_get_plan(const void* A, int64_t sAm, int64_t sAk, const void* B, int6
 int f16acc_flag_bytes_per_tile(void) { return kFlagBytesPerTile; }
 
 int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void* out, int device, void* stream) {
-    const bool known = (mode >= 0 && mode <= 15 && mode != 5) || (mode >= 20 && mode <= 28) || (mode >= 30 && mode <= 32);
+    const bool known = (mode >= 0 && mode <= 15 && mode != 5) || (mode >= 20 && mode <= 28) ||
+                       (mode >= 30 && mode <= 36) || (mode >= 40 && mode <= 43) || mode == 45;
     if (!known || chunks < 0 || grid <= 0 || out == nullptr) return F16ACC_ERR_INVALID_ARGUMENT;
     if (mode >= 2 && mode < 30 && epi_split != 2 && epi_split != 4) return F16ACC_ERR_INVALID_ARGUMENT;
     DeviceInfo* info = device_info(device);

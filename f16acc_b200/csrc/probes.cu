@@ -58,7 +58,8 @@ __global__ void __launch_bounds__(64 + 128 * EPI_SPLIT, 1) chunk_rate_kernel(int
     if (threadIdx.x == 0) {
         for (int b = 0; b < NBUF; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], (ProbeMode<MODE>::PER_THREAD ? 32 : 1) * 4 * EPI_SPLIT);
+            // mode 41: only the 8 warps that own a chunk (2 column slices x 4 quarters) release it
+            mbar_init(&tempty[b], MODE == 41 ? 8 : (ProbeMode<MODE>::PER_THREAD ? 32 : 1) * 4 * EPI_SPLIT);
         }
         mbar_init(done, 1);
         *abort_flag = 0;
@@ -90,6 +91,164 @@ __global__ void __launch_bounds__(64 + 128 * EPI_SPLIT, 1) chunk_rate_kernel(int
             if (!mbar_wait_drain(done, ph)) break;
             ph ^= 1u;
         }
+    } else if (MODE == 45 && warp == 1 && lane == 0) {
+        // wide chunks: 2 MMAs N=256 per chunk into 2 buffers of 256 columns
+        constexpr uint32_t idesc = idesc_f16(false, false, BM, 256);
+        uint32_t b = 0, ph = 0;
+        for (int c = 0; c < chunks; c += 2) {  // `chunks` counts 128-column chunks, 2 per wide chunk
+            if (!mbar_wait(&tempty[b], ph ^ 1u, abort_flag, status, kStatusTimeoutProbe)) break;
+            tc_fence_after();
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                umma_f16(tmem + b * 256, sdesc_sw128(a0 + h * 32, 16, 1024), sdesc_sw128(b0 + h * 32, 16, 1024),
+                         idesc, h);
+            umma_commit(&tfull[b]);
+            if (++b == 2) { b = 0; ph ^= 1u; }
+        }
+        umma_commit(done);
+        mbar_wait_drain(done, 0);
+    } else if (MODE == 45 && warp >= 2) {
+        const int e = warp - 2, q = warp & 3, colg = e >> 2;  // 16 warps: 4 slices of 64 over 256 columns
+        ChunkRing<2> ring{tfull, tempty, tmem + (static_cast<uint32_t>(q * 32) << 16) + colg * 64, 256};
+        float acc[64];
+#pragma unroll
+        for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
+        consume_chunks<64>(acc, chunks / 2, ring, lane, abort_flag, status);
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) s += acc[j];
+        out[blockIdx.x * blockDim.x + threadIdx.x] = s;
+    } else if ((MODE == 40 || MODE == 42 || MODE == 43) && warp == 1 && lane == 0) {
+        // pairs: one tempty wait, 4 MMAs into 2 chunk buffers, one commit per 2 chunks
+        constexpr uint32_t idesc = idesc_f16(false, false, BM, BN);
+        uint32_t p = 0, ph = 0;
+        for (int c = 0; c < chunks; c += 2, p ^= 1u) {
+            if (!mbar_wait(&tempty[p], ph ^ 1u, abort_flag, status, kStatusTimeoutProbe)) break;
+            tc_fence_after();
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                    umma_f16(tmem + (2 * p + k) * BN, sdesc_sw128(a0 + h * 32, 16, 1024),
+                             sdesc_sw128(b0 + h * 32, 16, 1024), idesc, h);
+            umma_commit(&tfull[p]);
+            if (p == 1) ph ^= 1u;
+        }
+        umma_commit(done);
+        mbar_wait_drain(done, 0);
+    } else if ((MODE == 40 || MODE == 42) && warp >= 2) {
+        const int e = warp - 2, q = warp & 3, colg = e >> 2;
+        const uint32_t base = tmem + (static_cast<uint32_t>(q * 32) << 16) + colg * CW;
+        float acc[CW];
+#pragma unroll
+        for (int j = 0; j < CW; ++j) acc[j] = 0.0f;
+        uint32_t p = 0, ph = 0;
+        for (int c = 0; c < chunks; c += 2, p ^= 1u) {
+            const bool ok = mbar_wait(&tfull[p], ph, abort_flag, status, kStatusTimeoutProbe);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            uint32_t r0[CW / 2], r1[CW / 2];
+            tmem_ld_chunk<CW>(base + (2 * p) * BN, r0);
+            tmem_ld_chunk<CW>(base + (2 * p + 1) * BN, r1);
+            tmem_wait_ld();
+            reg_fence(r0);
+            reg_fence(r1);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[p]);
+            add_chunk<CW>(acc, r0);
+            add_chunk<CW>(acc, r1);
+            if (p == 1) ph ^= 1u;
+        }
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < CW; ++j) s += acc[j];
+        out[blockIdx.x * blockDim.x + threadIdx.x] = s;
+    } else if (MODE == 43 && warp >= 2) {
+        // pairs, software pipelined: the next pair's loads are in flight while this pair is added
+        const int e = warp - 2, q = warp & 3, colg = e >> 2;
+        const uint32_t base = tmem + (static_cast<uint32_t>(q * 32) << 16) + colg * CW;
+        float acc[CW];
+#pragma unroll
+        for (int j = 0; j < CW; ++j) acc[j] = 0.0f;
+        uint32_t ra0[CW / 2], ra1[CW / 2], rb0[CW / 2], rb1[CW / 2];
+        uint32_t p = 0, ph = 0;
+        auto wait_pair = [&]() {
+            const bool ok = mbar_wait(&tfull[p], ph, abort_flag, status, kStatusTimeoutProbe);
+            if (!__all_sync(0xffffffffu, ok)) return false;
+            tc_fence_after();
+            return true;
+        };
+        auto release_pair = [&]() {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[p]);
+            if (p == 1) ph ^= 1u;
+            p ^= 1u;
+        };
+        const int pairs = chunks / 2;
+        if (pairs > 0 && wait_pair()) {
+            tmem_ld_chunk<CW>(base + (2 * p) * BN, ra0);
+            tmem_ld_chunk<CW>(base + (2 * p + 1) * BN, ra1);
+            for (int i = 0; i < pairs; i += 2) {
+                tmem_wait_ld();
+                reg_fence(ra0);
+                reg_fence(ra1);
+                release_pair();
+                const bool more = i + 1 < pairs;
+                if (more) {
+                    if (!wait_pair()) break;
+                    tmem_ld_chunk<CW>(base + (2 * p) * BN, rb0);
+                    tmem_ld_chunk<CW>(base + (2 * p + 1) * BN, rb1);
+                }
+                add_chunk<CW>(acc, ra0);
+                add_chunk<CW>(acc, ra1);
+                if (!more) break;
+                tmem_wait_ld();
+                reg_fence(rb0);
+                reg_fence(rb1);
+                release_pair();
+                const bool more2 = i + 2 < pairs;
+                if (more2) {
+                    if (!wait_pair()) break;
+                    tmem_ld_chunk<CW>(base + (2 * p) * BN, ra0);
+                    tmem_ld_chunk<CW>(base + (2 * p + 1) * BN, ra1);
+                }
+                add_chunk<CW>(acc, rb0);
+                add_chunk<CW>(acc, rb1);
+                if (!more2) break;
+            }
+        }
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < CW; ++j) s += acc[j];
+        out[blockIdx.x * blockDim.x + threadIdx.x] = s;
+    } else if (MODE == 41 && warp >= 2) {
+        // turn groups: two warps per (lane quarter, column slice) take alternate chunks
+        const int e = warp - 2, q = warp & 3, turn = (e >> 2) & 1, colg = e >> 3;
+        constexpr int CW41 = 64;
+        const uint32_t base = tmem + (static_cast<uint32_t>(q * 32) << 16) + colg * CW41;
+        float acc[CW41];
+#pragma unroll
+        for (int j = 0; j < CW41; ++j) acc[j] = 0.0f;
+        for (int c = turn; c < chunks; c += 2) {
+            const uint32_t b = c & (NBUF - 1), ph = (c / NBUF) & 1;
+            const bool ok = mbar_wait(&tfull[b], ph, abort_flag, status, kStatusTimeoutProbe);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            uint32_t r[CW41 / 2];
+            tmem_ld_chunk<CW41>(base + b * BN, r);
+            tmem_wait_ld();
+            reg_fence(r);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);
+            add_chunk<CW41>(acc, r);
+        }
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < CW41; ++j) s += acc[j];
+        out[blockIdx.x * blockDim.x + threadIdx.x] = s;
     } else if (MODE == 23 && warp >= 2) {
         // merged issuer: no MMA warp.  The epilogue warps read chunk c, meet at a
         // named barrier, and one of them issues chunk c+NBUF into the freed buffer.
@@ -293,6 +452,109 @@ __global__ void __launch_bounds__(256) mma_sync_rate_kernel(int iters, float* ou
     out[blockIdx.x * blockDim.x + threadIdx.x] = s;
 }
 
+// mma.sync fed from shared memory, the shape a register-accumulator GEMM would
+// use: 8 warps, each a 64 x 64 output tile (32 m16n8 tiles), per 32-long chunk
+// 16 ldmatrix.x4 (A 4 m-tiles x 2 k-halves, B 8 n-tiles x 2 k-halves), 64
+// mma.sync with an FP16 accumulator, 128 mixed adds into FP32 registers.
+// Operands are a fixed smem tile (A 128 x 32, B 256 x 32 K-contiguous,
+// padded rows).  33: as described; 34: the same without the FP32 adds (the
+// FP16 chunk results XOR-folded instead) to separate issue from smem costs.
+template <int MODE>
+__global__ void __launch_bounds__(256, 1) mma_sync_smem_kernel(int chunks, float* out) {
+    constexpr int LDK = 40;  // halves per smem row: 32 + 8 padding, conflict-free ldmatrix
+    __shared__ __align__(128) __half sA[128 * LDK];
+    __shared__ __align__(128) __half sB[256 * LDK];
+    for (int i = threadIdx.x; i < 128 * LDK; i += 256) sA[i] = __float2half((i & 3) == 0 ? 1.0f : 0.0f);
+    for (int i = threadIdx.x; i < 256 * LDK; i += 256) sB[i] = __float2half((i & 5) == 0 ? 1.0f : 0.0f);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int wm = warp >> 2, wn = warp & 3;  // 2 x 4 warps: rows wm*64, cols wn*64
+    float acc[4][8][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int v = 0; v < 4; ++v) acc[i][j][v] = 0.0f;
+    uint32_t fold = 0;
+    for (int c = 0; c < chunks; ++c) {
+        uint32_t af[2][4][4], bf[2][8][2];
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const __half* src = &sA[(wm * 64 + i * 16 + (lane & 15)) * LDK + ks * 16 + (lane >> 4) * 8];
+                asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                             : "=r"(af[ks][i][0]), "=r"(af[ks][i][1]), "=r"(af[ks][i][2]), "=r"(af[ks][i][3])
+                             : "r"(smem_u32(src)));
+            }
+#pragma unroll
+            for (int jp = 0; jp < 4; ++jp) {
+                const __half* src = &sB[(wn * 64 + jp * 16 + (lane >> 4) * 8 + (lane & 7)) * LDK + ks * 16 +
+                                        ((lane >> 3) & 1) * 8];
+                asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                             : "=r"(bf[ks][2 * jp][0]), "=r"(bf[ks][2 * jp][1]), "=r"(bf[ks][2 * jp + 1][0]),
+                               "=r"(bf[ks][2 * jp + 1][1])
+                             : "r"(smem_u32(src)));
+            }
+        }
+        if constexpr (MODE == 33 || MODE == 34) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    uint32_t h0 = 0, h1 = 0;
+#pragma unroll
+                    for (int ks = 0; ks < 2; ++ks)
+                        asm volatile(
+                            "mma.sync.aligned.m16n8k16.row.col.f16.f16.f16.f16 {%0,%1}, {%2,%3,%4,%5}, {%6,%7}, "
+                            "{%0,%1};"
+                            : "+r"(h0), "+r"(h1)
+                            : "r"(af[ks][i][0]), "r"(af[ks][i][1]), "r"(af[ks][i][2]), "r"(af[ks][i][3]),
+                              "r"(bf[ks][j][0]), "r"(bf[ks][j][1]));
+                    if constexpr (MODE == 33) {
+                        add_f16x2_to_f32(acc[i][j][0], acc[i][j][1], h0);
+                        add_f16x2_to_f32(acc[i][j][2], acc[i][j][3], h1);
+                    } else {
+                        fold ^= h0 ^ h1;
+                    }
+                }
+        } else {
+            // 35 / 36: groups of G tiles -- every tile's first K16 MMA, then every
+            // second one, then the adds -- so no MMA waits on the one just issued
+            constexpr int G = MODE == 35 ? 8 : 16;
+#pragma unroll
+            for (int g0 = 0; g0 < 32; g0 += G) {
+                uint32_t h[G][2];
+#pragma unroll
+                for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+                    for (int t = 0; t < G; ++t) {
+                        const int i = (g0 + t) >> 3, j = (g0 + t) & 7;
+                        if (ks == 0) h[t][0] = h[t][1] = 0u;
+                        asm("mma.sync.aligned.m16n8k16.row.col.f16.f16.f16.f16 {%0,%1}, {%2,%3,%4,%5}, {%6,%7}, "
+                            "{%0,%1};"
+                            : "+r"(h[t][0]), "+r"(h[t][1])
+                            : "r"(af[ks][i][0]), "r"(af[ks][i][1]), "r"(af[ks][i][2]), "r"(af[ks][i][3]),
+                              "r"(bf[ks][j][0]), "r"(bf[ks][j][1]));
+                    }
+#pragma unroll
+                for (int t = 0; t < G; ++t) {
+                    const int i = (g0 + t) >> 3, j = (g0 + t) & 7;
+                    add_f16x2_to_f32(acc[i][j][0], acc[i][j][1], h[t][0]);
+                    add_f16x2_to_f32(acc[i][j][2], acc[i][j][3], h[t][1]);
+                }
+            }
+        }
+    }
+    float s = __uint_as_float(fold);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += acc[i][j][0] + acc[i][j][1] + acc[i][j][2] + acc[i][j][3];
+    out[blockIdx.x * blockDim.x + threadIdx.x] = s;
+}
+
 namespace {
 template <int MODE, int EPI>
 cudaError_t launch_probe(int chunks, int grid, float* out, int* status, cudaStream_t stream) {
@@ -309,11 +571,15 @@ cudaError_t launch_probe(int chunks, int grid, float* out, int* status, cudaStre
 
 cudaError_t launch_chunk_rate(int mode, int epi_split, int chunks, int grid, float* out, int* status,
                               cudaStream_t stream) {
-    if (mode >= 30 && mode <= 32) {  // `grid` blocks of 8 warps; out holds grid * 256 floats
+    if (mode >= 30 && mode <= 36) {  // `grid` blocks of 8 warps; out holds grid * 256 floats
         switch (mode) {
             case 30: mma_sync_rate_kernel<30><<<grid, 256, 0, stream>>>(chunks, out); break;
             case 31: mma_sync_rate_kernel<31><<<grid, 256, 0, stream>>>(chunks, out); break;
             case 32: mma_sync_rate_kernel<32><<<grid, 256, 0, stream>>>(chunks, out); break;
+            case 33: mma_sync_smem_kernel<33><<<grid, 256, 0, stream>>>(chunks, out); break;
+            case 34: mma_sync_smem_kernel<34><<<grid, 256, 0, stream>>>(chunks, out); break;
+            case 35: mma_sync_smem_kernel<35><<<grid, 256, 0, stream>>>(chunks, out); break;
+            case 36: mma_sync_smem_kernel<36><<<grid, 256, 0, stream>>>(chunks, out); break;
         }
         return cudaGetLastError();
     }
@@ -343,6 +609,7 @@ cudaError_t launch_chunk_rate(int mode, int epi_split, int chunks, int grid, flo
             case 26: return launch_probe<26, 2>(chunks, grid, out, status, stream);
             case 27: return launch_probe<27, 2>(chunks, grid, out, status, stream);
             case 28: return launch_probe<28, 2>(chunks, grid, out, status, stream);
+            case 40: return launch_probe<40, 2>(chunks, grid, out, status, stream);
         }
     }
     if (epi_split == 4) {
@@ -351,6 +618,10 @@ cudaError_t launch_chunk_rate(int mode, int epi_split, int chunks, int grid, flo
             case 3: return launch_probe<3, 4>(chunks, grid, out, status, stream);
             case 6: return launch_probe<6, 4>(chunks, grid, out, status, stream);
             case 7: return launch_probe<7, 4>(chunks, grid, out, status, stream);
+            case 41: return launch_probe<41, 4>(chunks, grid, out, status, stream);
+            case 42: return launch_probe<42, 4>(chunks, grid, out, status, stream);
+            case 43: return launch_probe<43, 4>(chunks, grid, out, status, stream);
+            case 45: return launch_probe<45, 4>(chunks, grid, out, status, stream);
         }
     }
     return cudaErrorInvalidValue;

@@ -72,6 +72,53 @@ struct ChunkRing {
     }
 };
 
+// Chunk pairs: the MMA warp fills two chunk buffers (2p, 2p+1) per 64-wide
+// smem stage and signals them with one commit; the epilogue reads both and
+// releases them with one arrive.  Two pairs in flight (4 buffers).  Halving
+// the hand-offs per chunk is what pays: each hand-off costs a commit and two
+// barrier hops of latency, and only 4 chunk buffers fit in TMEM.
+template <int CW>
+struct PairRing {
+    uint64_t* tfull;   // [2]
+    uint64_t* tempty;  // [2]
+    uint32_t col_base; // TMEM address of buffer 0 for this warp's lanes and column slice
+    uint32_t stride;   // TMEM columns between chunk buffers
+    uint32_t p = 0, phase = 0;
+
+    __device__ __forceinline__ void advance() {
+        p ^= 1u;
+        if (p == 0) phase ^= 1u;
+    }
+};
+
+// Sum `nchunks` chunks, delivered in pairs, into acc (FP32).  The last pair of
+// a tile holds one chunk when nchunks is odd.  Returns false when a wait gave
+// up (no TMEM load is left in flight then).
+template <int CW>
+__device__ __forceinline__ bool consume_chunk_pairs(float (&acc)[CW], int nchunks, PairRing<CW>& ring, int lane,
+                                                    volatile int* abort, int* status) {
+    for (int c = 0; c < nchunks; c += 2) {
+        const bool ok = mbar_wait(&ring.tfull[ring.p], ring.phase, abort, status, kStatusTimeoutEpilogue);
+        if (!__all_sync(0xffffffffu, ok)) return false;
+        tc_fence_after();
+        const bool two = c + 1 < nchunks;
+        const uint32_t a0 = ring.col_base + (2 * ring.p) * ring.stride;
+        uint32_t r0[CW / 2], r1[CW / 2];
+        tmem_ld_chunk<CW>(a0, r0);
+        if (two) tmem_ld_chunk<CW>(a0 + ring.stride, r1);
+        tmem_wait_ld();
+        reg_fence(r0);
+        if (two) reg_fence(r1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ring.tempty[ring.p]);
+        ring.advance();
+        add_chunk<CW>(acc, r0);
+        if (two) add_chunk<CW>(acc, r1);
+    }
+    return true;
+}
+
 // Sum `nchunks` chunk accumulators into acc (FP32), consuming them from the
 // ring in order.  Returns false when a wait gave up (nothing in flight then).
 template <int CW, typename Ring>

@@ -173,16 +173,17 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT>::THREADS, 1)
                 raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
                 if (REDO && !tile_flagged(p.flags, static_cast<int64_t>(tm) * p.tiles_n + tn)) continue;
                 if constexpr (CHUNKED) {
+                    // One hand-off per 64-wide stage: its two 32-long chunks go to the
+                    // chunk buffers 2b and 2b+1 of pair b (two pairs in flight), one commit.
                     for (int kb = 0; kb < nkb; ++kb) {
                         if (!mbar_wait(&full[s], ph, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
+                        if (!mbar_wait(&tempty[b], tph ^ 1u, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
                         tc_fence_after();
 #pragma unroll
                         for (int cc = 0; cc < 2; ++cc) {
                             const int c = kb * 2 + cc;
                             if (c >= nchunks) break;
-                            if (!mbar_wait(&tempty[b], tph ^ 1u, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
-                            tc_fence_after();
-                            const uint32_t d = tmem + b * Cfg::ACC_COLS;
+                            const uint32_t d = tmem + (2 * b + cc) * Cfg::ACC_COLS;
 #pragma unroll
                             for (int h = 0; h < 2; ++h) {
                                 const int ks = cc * 2 + h;
@@ -192,10 +193,11 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT>::THREADS, 1)
                                                          : sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 32, 16, 1024);
                                 umma_f16(d, ad, bd, idesc, h);
                             }
-                            umma_commit(&tfull[b]);
-                            if (++b == NBUF) { b = 0; tph ^= 1u; }
                         }
+                        umma_commit(&tfull[b]);
                         umma_commit(&empty[s]);
+                        b ^= 1u;
+                        if (b == 0) tph ^= 1u;
                         if (++s == STAGES) { s = 0; ph ^= 1u; }
                     }
                 } else {
@@ -232,7 +234,8 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT>::THREADS, 1)
         const int q = warp & 3;          // TMEM lane quarter this warp may access
         const int colg = e >> 2;         // column slice
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-        ChunkRing<NBUF> ring{tfull, tempty, tmem + lane_base + colg * CW, Cfg::ACC_COLS};
+        ChunkRing<NBUF> ring{tfull, tempty, tmem + lane_base + colg * CW, Cfg::ACC_COLS};    // FP32 mode
+        PairRing<CW> pairs{tfull, tempty, tmem + lane_base + colg * CW, Cfg::ACC_COLS};     // chunked mode
         for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
             int tm, tn;
             raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
@@ -242,7 +245,7 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT>::THREADS, 1)
             if constexpr (CHUNKED) {
 #pragma unroll
                 for (int j = 0; j < CW; ++j) acc[j] = 0.0f;
-                if (!consume_chunks<CW>(acc, nchunks, ring, lane, abort_flag, p.status)) break;
+                if (!consume_chunk_pairs<CW>(acc, nchunks, pairs, lane, abort_flag, p.status)) break;
                 float z = 0.0f;
 #pragma unroll
                 for (int j = 0; j < CW; ++j) z = nonfinite_probe(z, acc[j]);

@@ -67,7 +67,10 @@ def main(argv=None) -> int:
               ("pingpong_no_mma_8slots", 20, 2), ("mma_f16acc_n64", 21, 2), ("mma_f16acc_n256", 22, 2),
               ("chunk_pipeline_merged_issuer", 23, 2), ("pingpong_no_fence", 24, 2),
               ("pingpong_per_thread_arrive", 25, 2), ("pingpong_no_fence_per_thread", 26, 2),
-              ("handoff_per_thread_arrive", 27, 2), ("mma_issue_commit_only", 28, 2)]
+              ("handoff_per_thread_arrive", 27, 2), ("mma_issue_commit_only", 28, 2),
+              ("chunk_pipeline_pairs", 40, 2), ("chunk_pipeline_turn_groups_16warp", 41, 4),
+              ("chunk_pipeline_pairs_16warp", 42, 4), ("chunk_pipeline_pairs_16warp_pipelined", 43, 4),
+              ("chunk_pipeline_wide_n256_16warp", 45, 4)]
     for name, mode, epi in probes:
         sms, ms, tflops, clk = run(mode, epi, a.chunks, a.reps, dev)
         mhz = clk.get("sm_mhz")
@@ -75,10 +78,12 @@ def main(argv=None) -> int:
         print(json.dumps({"probe": name, "chunks_per_cta": a.chunks, "ms": ms, "tflops": tflops, "clocks": clk,
                           "frac_of_clock_peak": tflops / peak if peak else None}), flush=True)
     # warp-level mma.sync: 4 blocks of 8 warps per SM, 8 independent chains per warp
-    for name, mode in (("mma_sync_f16acc", 30), ("mma_sync_f32acc", 31), ("mma_sync_chunk32", 32)):
+    for name, mode in (("mma_sync_f16acc", 30), ("mma_sync_f32acc", 31), ("mma_sync_chunk32", 32),
+                       ("mma_sync_smem_64x64_chunked", 33), ("mma_sync_smem_64x64_no_adds", 34),
+                       ("mma_sync_smem_64x64_grouped8", 35), ("mma_sync_smem_64x64_grouped16", 36)):
         lib = _lib.load()
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
-        grid = 4 * sms
+        grid = 4 * sms if mode <= 32 else sms
         out = torch.empty(grid * 256, device=dev)
         iters = max(1024, a.chunks // 4)
         stream = torch.cuda.current_stream(dev)
@@ -98,8 +103,8 @@ def main(argv=None) -> int:
             e1.record(stream)
             torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / a.reps
-        steps = 2 if mode == 32 else 1
-        tflops = grid * 8 * iters * steps * 8 * 4096 / (ms / 1e3) / 1e12
+        mmas_per_warp_iter = {30: 8, 31: 8, 32: 16, 33: 64, 34: 64, 35: 64, 36: 64}[mode]
+        tflops = grid * 8 * iters * mmas_per_warp_iter * 4096 / (ms / 1e3) / 1e12
         clk = clocks.summary()
         mhz = clk.get("sm_mhz")
         peak = sms * 8192 * mhz * 1e6 / 1e12 if mhz else None

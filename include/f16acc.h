@@ -145,10 +145,18 @@ int f16acc_set_tc_config(int tile_n, int epi_split);
  * instructions; 23 = chunk pipeline whose epilogue warps issue the next
  * chunk's MMAs themselves after a named barrier.  24 / 25 / 26 = ping-pong
  * without tcgen05 fences / with per-thread arrives / both; 27 = mode 4 with
- * per-thread arrives; 28 = MMA issue with a commit per chunk, no waiting.
+ * per-thread arrives; 28 = MMA issue with a commit per chunk, no waiting;
+ * 40 = chunk pipeline handing chunks over in pairs (one commit / release per
+ * two chunks); 41 = chunk pipeline with 16 epilogue warps, two per (lane
+ * quarter, column slice) taking alternate chunks (epi_split 4); 42 / 43 =
+ * pairs with 16 epilogue warps, plain / software pipelined (epi_split 4);
+ * 45 = 128x256 chunks (N=256 MMAs, 2 TMEM buffers), 16 epilogue warps.
  * Warp-level mma.sync rate (grid blocks of 8
  * warps, 8 m16n8k16 chains per warp, `chunks` iterations): 30 = FP16
- * accumulate, 31 = FP32 accumulate, 32 = FP16 chunks of 2 steps added into FP32.
+ * accumulate, 31 = FP32 accumulate, 32 = FP16 chunks of 2 steps added into FP32;
+ * 33 / 34 = fed from shared memory by ldmatrix, 64x64 warp tiles, with / without
+ * the FP32 adds (one block of 8 warps per SM); 35 / 36 = the same issuing each
+ * group of 8 / 16 tiles' first K16 MMAs before their second ones.
  * `out` is device memory for grid * max(256, 64 + 128*epi_split) floats.
  * Asynchronous on `stream`; time it with events. */
 int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void *out, int device, void *stream);
