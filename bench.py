@@ -128,16 +128,20 @@ def cpu_sample(rows: int, seed: int = 1):
 
 
 def cpu_threads():
-    n = os.environ.get("OMP_NUM_THREADS")
-    return int(n) if n else (os.cpu_count() or 1)
+    """Give the CPU path every host thread (torchrun pins OMP_NUM_THREADS=1)
+    and report the count in effect."""
+    from oracle import oracle as O
+
+    return O.set_threads(len(os.sched_getaffinity(0)) or os.cpu_count() or 1)
 
 
 def cpu_baseline(target_s: float = 10.0):
     """Chunked emulation of rows of the 4096^3 product, sized to ~target_s."""
+    cores = cpu_threads()
     dt, _ = cpu_sample(16)
     rows = int(max(16, min(M, 16 * target_s / max(dt, 1e-3))))
     dt, tflops = cpu_sample(rows)
-    return {"value": tflops, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+    return {"value": tflops, "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"oracle chunked emulation (oracle/f16acc_oracle.c, OpenMP) of {rows} of the 4096 rows "
                       f"of one 4096^3 product: {dt:.1f} s"}
 
@@ -147,6 +151,7 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    cores = cpu_threads()
     # size each step so the whole --steps/--warmup run stays within ~2 minutes
     dt16, _ = cpu_sample(16)
     budget = 120.0 / max(1, args.steps + args.warmup)
@@ -165,7 +170,7 @@ def run_reference(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
         "config": {"workload": "config 2: 4096^3 fp16 GEMM, N(0,1)/sqrt(K)*4, chunked FP16 accumulate",
                    "rows_per_step": rows},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": f"{rows} rows of the 4096^3 product per step (reference chunked semantics, "
                                    "oracle/f16acc_oracle.c)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -335,6 +340,87 @@ def run_ours(args):
     return 0
 
 
+def rel_err(x, ref) -> float:
+    return ((x.double() - ref).abs().max() / ref.abs().max()).item()
+
+
+def run_workload(args):
+    """The other BASELINE configs (f16acc_b200/workloads.py): one JSON line each."""
+    import torch
+
+    from f16acc_b200 import workloads as W
+
+    want_nccl = args.workload in ("nshard", "prefill")
+    world, rank, local = dist_setup(torch, want_nccl=want_nccl)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    line = {"workload": args.workload, "n_gpus": world, "data": "synthetic"}
+    if args.workload == "shapes":
+        line["config"] = "config 3: Qwen2.5-1.5B linear shapes, M=2048, weight [N,K], fp16 out"
+        line["results"] = W.shapes(dev)
+    elif args.workload == "overflow":
+        line["config"] = "config 4: 4096^3 N(0,1), 1% rows/cols x64; 4b: ~1% of tiles overflow"
+        line["results"] = W.overflow(dev)
+    elif args.workload == "nshard":
+        from f16acc_b200.kernel import mm
+        from f16acc_b200.shard import nshard_mm, shard_bounds
+
+        n = args.size
+        g = torch.Generator(device=dev).manual_seed(3)  # same A and B on every rank
+        a = torch.randn(n, n, device=dev, generator=g).half()
+        b = torch.randn(n, n, device=dev, generator=g).half()
+        lo, hi = shard_bounds(n, world, rank)
+        b_shard = b[:, lo:hi].contiguous()
+
+        def step(gather=True):
+            if world == 1:
+                return mm(a, b_shard)
+            return nshard_mm(a, b_shard, gather=gather)
+
+        times = {}
+        for mode in ("compute_only", "with_allgather"):
+            gather = mode == "with_allgather"
+            for _ in range(max(3, args.warmup)):
+                step(gather)
+            torch.cuda.synchronize()
+            barrier(torch, world)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                c = step(gather)
+            e1.record()
+            torch.cuda.synchronize()
+            barrier(torch, world)
+            times[mode] = max_over_ranks(torch, e0.elapsed_time(e1) / args.steps, world, dev)
+        # the (gathered) C is the full product: check the first 64 rows against FP64
+        ref = a[:64].double() @ b.double()
+        line["max_rel_err_first_64_rows"] = max_over_ranks(torch, rel_err(c[:64], ref), world, dev)
+        del ref
+        line["config"] = f"config 4c: N-sharded {n}^3 fp16 over {world} ranks, NCCL all-gather of C"
+        flops = 2.0 * n ** 3
+        line["results"] = {k: {"ms": v, "tflops": flops / v / 1e9} for k, v in times.items()}
+        line["scaling"] = "strong"
+    elif args.workload == "prefill":
+        r = W.prefill(dev, rank=rank, world=world)
+        ms_c = max_over_ranks(torch, r["ms_cublas"], world, dev)
+        ms_f = max_over_ranks(torch, r["ms_f16acc"], world, dev)
+        tokens = 8 * 2048
+        line["config"] = ("config 5: random-init Qwen2.5-1.5B architecture (28 layers, hidden 1536, 12/2 heads, "
+                          "intermediate 8960, vocab 151936, tied), 8 prompts x 2048 tokens, data parallel")
+        line["results"] = {"tokens_per_s_f16acc": tokens / (ms_f / 1e3), "tokens_per_s_cublas": tokens / (ms_c / 1e3),
+                           "speedup": ms_c / ms_f, "top1_agreement_rank0": r["top1_agreement"],
+                           "routed_calls_per_pass_rank0": r["routed_calls_per_pass"]}
+        line["scaling"] = "strong"
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description="f16acc B200 benchmark")
     ap.add_argument("--gpus", type=int, default=1)
@@ -342,9 +428,14 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--variant", choices=["auto", "tcgen05", "mma_sync"], default="auto")
+    ap.add_argument("--workload", choices=["gemm4096", "shapes", "overflow", "nshard", "prefill"], default="gemm4096",
+                    help="gemm4096 is the headline line; the others print their own JSON line")
+    ap.add_argument("--size", type=int, default=16384, help="matrix size for --workload nshard")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload != "gemm4096":
+        return run_workload(args)
     return run_ours(args)
 
 

@@ -37,6 +37,7 @@ SIGNATURES = {
     "f16acc_get_plan": (_int, [_p, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _int, ctypes.POINTER(Plan)]),
     "f16acc_flag_bytes_per_tile": (_int, []),
     "f16acc_set_tc_config": (_int, [_int, _int]),
+    "f16acc_set_sm_limit": (_int, [_int]),
     "f16acc_probe_chunk_rate": (_int, [_int, _int, _int, _int, _p, _int, _p]),
     "f16acc_device_status": (_int, [_int, _int]),
     "f16acc_gemm_noalloc": (_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _int, _i64, _i64, _i64, _int,

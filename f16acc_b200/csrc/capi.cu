@@ -117,6 +117,15 @@ Layout analyse(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t s
 // slices per TMEM lane quarter.  Process-wide; f16acc_set_tc_config changes
 // it (tuning and measurement), calls already issued keep theirs.
 std::atomic<int> g_tc_bn{128}, g_tc_epi{2};
+
+// Upper bound on the SMs a persistent launch may occupy (0 = all).  Leaving a
+// few SMs free lets kernels on other streams -- NCCL collectives overlapping a
+// sharded product -- run alongside instead of queueing behind the GEMM.
+std::atomic<int> g_sm_limit{0};
+int usable_sms(int sms) {
+    const int lim = g_sm_limit.load(std::memory_order_relaxed);
+    return lim > 0 && lim < sms ? lim : sms;
+}
 TcShape tc_shape() { return TcShape{g_tc_bn.load(std::memory_order_relaxed), g_tc_epi.load(std::memory_order_relaxed)}; }
 constexpr int kGroupM = 8;
 
@@ -213,7 +222,8 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
         p.flags = static_cast<uint8_t*>(workspace);
         p.status = info->status;
         const int64_t tiles = int64_t(p.tiles_m) * p.tiles_n;
-        const int grid = int(tiles < info->sms ? tiles : info->sms);
+        const int sms = usable_sms(info->sms);
+        const int grid = int(tiles < sms ? tiles : sms);
         if ((phases & kPhaseMain) &&
             launch_tc(p, shape, chunked != 0, b_mn, c_dtype, false, grid, stream) != cudaSuccess)
             return F16ACC_ERR_CUDA;
@@ -250,7 +260,8 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
         launch_mma(q, chunked != 0, a_mode, b_mode, c_dtype, false, int(tiles), stream) != cudaSuccess)
         return F16ACC_ERR_CUDA;
     if (chunked && (phases & kPhaseRedo)) {
-        const int64_t redo_grid = tiles < 2 * info->sms ? tiles : 2 * info->sms;
+        const int64_t sms2 = 2 * int64_t(usable_sms(info->sms));
+        const int64_t redo_grid = tiles < sms2 ? tiles : sms2;
         if (launch_mma(q, false, a_mode, b_mode, c_dtype, true, int(redo_grid), stream) != cudaSuccess)
             return F16ACC_ERR_CUDA;
     }
@@ -345,6 +356,12 @@ int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void*
                              static_cast<cudaStream_t>(stream)) == cudaSuccess
                ? F16ACC_OK
                : F16ACC_ERR_CUDA;
+}
+
+int f16acc_set_sm_limit(int max_sms) {
+    if (max_sms < 0) return F16ACC_ERR_INVALID_ARGUMENT;
+    const int prev = g_sm_limit.exchange(max_sms);
+    return prev;
 }
 
 int f16acc_set_tc_config(int tile_n, int epi_split) {

@@ -47,7 +47,8 @@ def _default_mm(a, b, out_dtype):
 
 def nshard_mm(a: torch.Tensor, b_shard: torch.Tensor, *, gather: bool = True, row_major: bool = True,
               out_dtype=torch.float16, blocks: int = 4, group=None,
-              mm_fn: Optional[Callable] = None, comm_stream: Optional[torch.cuda.Stream] = None):
+              mm_fn: Optional[Callable] = None, comm_stream: Optional[torch.cuda.Stream] = None,
+              reserve_sms: int = 16):
     """C = A @ B with B column-sharded across the ranks of `group`.
 
     Every rank passes the full A [M, K] and its own B column slice [K, N/P]
@@ -55,8 +56,12 @@ def nshard_mm(a: torch.Tensor, b_shard: torch.Tensor, *, gather: bool = True, ro
     `gather` is False; otherwise all panels, either rank-blocked [P, M, N/P]
     (`row_major=False`) or as row-major [M, N].  The gather runs per row block
     (`blocks` of them) so block i's exchange overlaps block i+1's compute.
-    `mm_fn(a, b, out_dtype)` defaults to the chunked kernel.
+    `mm_fn(a, b, out_dtype)` defaults to the chunked kernel; while it runs
+    with gathers in flight, the kernel is capped to all but `reserve_sms` SMs
+    (the GEMM is persistent, one CTA per SM, and would otherwise keep NCCL's
+    kernels from being scheduled until it finished).
     """
+    default_kernel = mm_fn is None
     mm_fn = mm_fn or _default_mm
     M = a.shape[0]
     n_local = b_shard.shape[1]
@@ -90,20 +95,31 @@ def nshard_mm(a: torch.Tensor, b_shard: torch.Tensor, *, gather: bool = True, ro
             out[:, r0:r1].copy_(recv)
         return recv
 
-    for i in range(blocks):
-        r0, r1 = shard_bounds(M, blocks, i)
-        panel = mm_fn(a[r0:r1], b_shard, out_dtype).contiguous()
-        if use_streams:
-            ev = torch.cuda.Event()
-            ev.record(compute)
-            comm.wait_event(ev)
-            with torch.cuda.stream(comm):
-                recv = exchange(panel, r0, r1)
-            # buffers made on the compute stream and used on comm stay allocated until comm is done
-            panel.record_stream(comm)
-            recv.record_stream(comm)
-        else:
-            exchange(panel, r0, r1)
+    lib = None
+    if use_streams and default_kernel and reserve_sms > 0:
+        from . import _lib
+
+        lib = _lib.load()
+        sms = torch.cuda.get_device_properties(a.device).multi_processor_count
+        prev_limit = lib.f16acc_set_sm_limit(max(1, sms - reserve_sms))
+    try:
+        for i in range(blocks):
+            r0, r1 = shard_bounds(M, blocks, i)
+            panel = mm_fn(a[r0:r1], b_shard, out_dtype).contiguous()
+            if use_streams:
+                ev = torch.cuda.Event()
+                ev.record(compute)
+                comm.wait_event(ev)
+                with torch.cuda.stream(comm):
+                    recv = exchange(panel, r0, r1)
+                # buffers made on the compute stream and used on comm stay allocated until comm is done
+                panel.record_stream(comm)
+                recv.record_stream(comm)
+            else:
+                exchange(panel, r0, r1)
+    finally:
+        if lib is not None:
+            lib.f16acc_set_sm_limit(prev_limit)
     if use_streams:
         done = torch.cuda.Event()
         done.record(comm)

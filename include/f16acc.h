@@ -130,6 +130,12 @@ int f16acc_flag_bytes_per_tile(void);
  * f16acc_gemm_main and its f16acc_gemm_redo. */
 int f16acc_set_tc_config(int tile_n, int epi_split);
 
+/* Cap the SMs a GEMM launch occupies, process-wide, for later calls (0 = all
+ * SMs, the default).  The GEMM kernels are persistent (one CTA per SM); a cap
+ * leaves SMs free for kernels on other streams, such as an NCCL collective
+ * that overlaps a sharded product.  Returns the previous cap. */
+int f16acc_set_sm_limit(int max_sms);
+
 /* Raw-rate probe, the B200 counterpart of the reference's bench/rate.py and
  * bench/chunkrate.py: `grid` CTAs (one per SM) each run `chunks` 32-long
  * chunks of 128x128 tcgen05 MMAs on a fixed shared-memory tile.  mode 0: MMA

@@ -36,6 +36,7 @@
  * 65536-entry table, so the inner loops are plain float/double arithmetic.
  */
 #include <math.h>
+#include <omp.h>
 #include <pthread.h>
 #include <stdint.h>
 #include <stdlib.h>
@@ -213,6 +214,13 @@ void oracle_gemm_chunked(const uint16_t *A, int64_t sAm, int64_t sAk,
 void oracle_round_f16(const float *in, uint16_t *out, int64_t n) {
     for (int64_t i = 0; i < n; ++i) out[i] = f2h((double)in[i]);
 }
+
+/* OpenMP threads the oracle uses (set / query); a launcher such as torchrun
+ * may have pinned OMP_NUM_THREADS to 1 for the process. */
+void oracle_set_threads(int n) {
+    if (n > 0) omp_set_num_threads(n);
+}
+int oracle_threads(void) { return omp_get_max_threads(); }
 
 /* rel() of tests/test_f16acc.py:11-12 for an FP32 candidate; NaN propagates. */
 double oracle_rel(const float *x, const double *ref, int64_t n) {

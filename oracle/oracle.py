@@ -47,6 +47,8 @@ def lib():
         L.oracle_round_f16.argtypes = [_p, _p, _i64]
         L.oracle_rel.argtypes = [_p, _p, _i64]
         L.oracle_rel.restype = ctypes.c_double
+        L.oracle_set_threads.argtypes = [ctypes.c_int]
+        L.oracle_threads.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -130,6 +132,17 @@ def round_f16(x: np.ndarray) -> np.ndarray:
     out = np.empty(x.shape, dtype=np.float16)
     lib().oracle_round_f16(x.ctypes.data, out.ctypes.data, x.size)
     return out
+
+
+def set_threads(n: int) -> int:
+    """Use n OpenMP threads (e.g. os.cpu_count() under a launcher that pinned
+    OMP_NUM_THREADS=1); returns the count now in effect."""
+    lib().oracle_set_threads(int(n))
+    return int(lib().oracle_threads())
+
+
+def threads() -> int:
+    return int(lib().oracle_threads())
 
 
 def rel(x: np.ndarray, ref: np.ndarray) -> float:
