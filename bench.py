@@ -372,26 +372,44 @@ def run_workload(args):
         lo, hi = shard_bounds(n, world, rank)
         b_shard = b[:, lo:hi].contiguous()
 
-        def step(gather=True):
+        def step(gather=True, blocks=args.nshard_blocks, reserve=args.nshard_reserve):
             if world == 1:
                 return mm(a, b_shard)
-            return nshard_mm(a, b_shard, gather=gather)
+            return nshard_mm(a, b_shard, gather=gather, blocks=blocks, reserve_sms=reserve)
 
-        times = {}
-        for mode in ("compute_only", "with_allgather"):
-            gather = mode == "with_allgather"
+        def timed(fn):
             for _ in range(max(3, args.warmup)):
-                step(gather)
+                fn()
             torch.cuda.synchronize()
             barrier(torch, world)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             for _ in range(args.steps):
-                c = step(gather)
+                r = fn()
             e1.record()
             torch.cuda.synchronize()
             barrier(torch, world)
-            times[mode] = max_over_ranks(torch, e0.elapsed_time(e1) / args.steps, world, dev)
+            return max_over_ranks(torch, e0.elapsed_time(e1) / args.steps, world, dev), r
+
+        times = {}
+        times["compute_only"], c = timed(lambda: step(False))
+        times["with_allgather"], c = timed(lambda: step(True))
+        if world > 1:
+            from f16acc_b200.shard import nshard_mm_fused
+
+            times["fused_gemm_allgather"], c = timed(lambda: nshard_mm_fused(a, b_shard))
+        if world > 1 and args.nshard_sweep:
+            import torch.distributed as dist
+
+            panel = torch.empty(n, hi - lo, dtype=torch.float16, device=dev)
+            flat = torch.empty(world * n, hi - lo, dtype=torch.float16, device=dev)
+            t_ag, _ = timed(lambda: dist.all_gather_into_tensor(flat, panel))
+            times["allgather_only"] = t_ag
+            line["allgather_bus_gbs"] = (world - 1) * panel.numel() * 2 / (t_ag / 1e3) / 1e9
+            for blocks in (1, 2, 8):
+                for reserve in (0, 16):
+                    times[f"with_allgather_blocks{blocks}_reserve{reserve}"], _ = timed(
+                        lambda: step(True, blocks, reserve))
         # the (gathered) C is the full product: check the first 64 rows against FP64
         ref = a[:64].double() @ b.double()
         line["max_rel_err_first_64_rows"] = max_over_ranks(torch, rel_err(c[:64], ref), world, dev)
@@ -431,6 +449,9 @@ def main(argv=None):
     ap.add_argument("--workload", choices=["gemm4096", "shapes", "overflow", "nshard", "prefill"], default="gemm4096",
                     help="gemm4096 is the headline line; the others print their own JSON line")
     ap.add_argument("--size", type=int, default=16384, help="matrix size for --workload nshard")
+    ap.add_argument("--nshard-blocks", type=int, default=4, help="row blocks the sharded gather is pipelined in")
+    ap.add_argument("--nshard-reserve", type=int, default=16, help="SMs left free for NCCL during the product")
+    ap.add_argument("--nshard-sweep", action="store_true", help="also time the bare all-gather and other blockings")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)

@@ -116,7 +116,7 @@ Layout analyse(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t s
 // tcgen05 tile configuration: output columns per tile and epilogue column
 // slices per TMEM lane quarter.  Process-wide; f16acc_set_tc_config changes
 // it (tuning and measurement), calls already issued keep theirs.
-std::atomic<int> g_tc_bn{128}, g_tc_epi{2};
+std::atomic<int> g_tc_bn{128}, g_tc_epi{4};
 
 // Upper bound on the SMs a persistent launch may occupy (0 = all).  Leaving a
 // few SMs free lets kernels on other streams -- NCCL collectives overlapping a
@@ -161,7 +161,10 @@ struct DeviceGuard {
 
 int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int64_t sBn, void* C, int64_t sCm,
         int64_t sCn, int c_dtype, int64_t M, int64_t N, int64_t K, int chunked, void* workspace, size_t ws_bytes,
-        int device, void* stream_ptr, int variant, int phases) {
+        int device, void* stream_ptr, int variant, int phases, void* const* peers = nullptr, int n_peers = 0) {
+    if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && peers == nullptr)) return F16ACC_ERR_INVALID_ARGUMENT;
+    for (int i = 0; i < n_peers; ++i)
+        if (peers[i] == nullptr) return F16ACC_ERR_INVALID_ARGUMENT;
     if (M < 0 || N < 0 || K < 0) return F16ACC_ERR_INVALID_ARGUMENT;
     if (c_dtype != F16ACC_OUT_F16 && c_dtype != F16ACC_OUT_F32 && c_dtype != F16ACC_OUT_BF16)
         return F16ACC_ERR_INVALID_ARGUMENT;
@@ -218,9 +221,13 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
         p.tiles_m = int(cdiv(M, 128));
         p.tiles_n = int(cdiv(N, bn));
         p.group_m = kGroupM;
-        p.c_vec = (sCn == 1 && pc % 16 == 0 && (sCm * esize) % 16 == 0) ? 1 : 0;
+        bool aligned = pc % 16 == 0;
+        for (int i = 0; i < n_peers; ++i) aligned = aligned && reinterpret_cast<uintptr_t>(peers[i]) % 16 == 0;
+        p.c_vec = (sCn == 1 && aligned && (sCm * esize) % 16 == 0) ? 1 : 0;
         p.flags = static_cast<uint8_t*>(workspace);
         p.status = info->status;
+        p.n_peers = n_peers;
+        for (int i = 0; i < n_peers; ++i) p.peers[i] = peers[i];
         const int64_t tiles = int64_t(p.tiles_m) * p.tiles_n;
         const int sms = usable_sms(info->sms);
         const int grid = int(tiles < sms ? tiles : sms);
@@ -233,6 +240,7 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
         return F16ACC_OK;
     }
 
+    if (n_peers > 0) return F16ACC_ERR_UNSUPPORTED;  // peer stores: tcgen05 path only
     MmaParams q;
     std::memset(&q, 0, sizeof(q));
     q.A = static_cast<const __half*>(A);
@@ -301,6 +309,14 @@ int f16acc_gemm_redo(const void* A, int64_t sAm, int64_t sAk, const void* B, int
                      void* workspace, size_t ws_bytes, int device, void* stream, int variant) {
     return run(A, sAm, sAk, B, sBk, sBn, C, sCm, sCn, c_dtype, M, N, K, chunked, workspace, ws_bytes, device, stream,
                variant, kPhaseRedo);
+}
+
+int f16acc_gemm_allgather(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int64_t sBn,
+                          void* const* outs, int n_outs, int64_t sCm, int64_t sCn, int c_dtype, int64_t M, int64_t N,
+                          int64_t K, int chunked, void* workspace, size_t ws_bytes, int device, void* stream) {
+    if (outs == nullptr || n_outs < 1 || n_outs > kMaxPeers + 1) return F16ACC_ERR_INVALID_ARGUMENT;
+    return run(A, sAm, sAk, B, sBk, sBn, outs[0], sCm, sCn, c_dtype, M, N, K, chunked, workspace, ws_bytes, device,
+               stream, F16ACC_VARIANT_TCGEN05, kPhaseBoth, outs + 1, n_outs - 1);
 }
 
 size_t f16acc_workspace_bytes(int64_t M, int64_t N, int64_t K) {

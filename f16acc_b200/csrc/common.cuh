@@ -18,6 +18,9 @@ enum OutType : int { kOutF16 = 0, kOutF32 = 1, kOutBF16 = 2 };
 // grid (tile_m * tiles_n + tile_n), independent of the raster order.
 constexpr int kFlagBytesPerTile = 16;
 
+// Most peer outputs a fused GEMM + all-gather call stores to (8 GPUs per node).
+constexpr int kMaxPeers = 7;
+
 // Grouped raster: `group_m` consecutive tile rows are walked column by column,
 // so the CTAs that run at the same time share A row-panels and B column-panels
 // in L2.  Maps the linear schedule index t to (tile_m, tile_n).

@@ -45,6 +45,12 @@ struct TcParams {
     int c_vec;        // C rows allow 16-byte vector stores
     uint8_t* flags;   // kFlagBytesPerTile per tile
     int* status;      // device status word (timeouts)
+    // Fused all-gather: each finished tile is also stored, at the same element
+    // offsets and strides, into these peer buffers (another GPU's memory mapped
+    // into this process, written over NVLink by plain stores).  0 peers = a
+    // plain GEMM.
+    int n_peers;
+    void* peers[kMaxPeers];
 };
 
 template <int BN_, int EPI_SPLIT_>
@@ -273,7 +279,12 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT>::THREADS, 1)
             const int row = tm * BM + q * 32 + lane;
             const int col0 = tn * BN + colg * CW;
             store_row<OUT, CW>(p.C, p.sCm, p.sCn, row, col0, p.M, p.N, acc, p.c_vec != 0);
+            // fused all-gather: the same tile into every peer's buffer, over NVLink
+            for (int i = 0; i < p.n_peers; ++i)
+                store_row<OUT, CW>(p.peers[i], p.sCm, p.sCn, row, col0, p.M, p.N, acc, p.c_vec != 0);
         }
+        // peer stores become visible system-wide before the kernel is seen complete
+        if (p.n_peers > 0) __threadfence_system();
     }
 
     tc_fence_before();

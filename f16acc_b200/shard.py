@@ -9,6 +9,10 @@ Two ways the product shards across the GPUs of one node:
   gather is pipelined by row blocks on a side stream so it overlaps the next
   block's compute; the gathered buffer is [P, M, N/P] (rank-blocked) and is
   either returned as is or permuted into row-major [M, N] on the device.
+* N-column shards, fused (`nshard_mm_fused`): the GEMM kernel itself stores
+  every finished tile into all ranks' row-major outputs over NVLink (peer
+  memory from torch symmetric memory), so the exchange overlaps the math tile
+  by tile and needs no SMs of its own; a device barrier ends the call.
 * M-row shards (`mshard_rows`): token batches are independent, so each rank
   takes a contiguous block of rows and needs no collective at all.
 
@@ -18,6 +22,7 @@ new.  Every rank issues the same collectives in the same order.
 
 from __future__ import annotations
 
+import ctypes
 from typing import Callable, Optional
 
 import torch
@@ -37,6 +42,67 @@ def mshard_rows(x: torch.Tensor, rank: int, world: int) -> torch.Tensor:
     """This rank's contiguous block of rows (independent token batches)."""
     lo, hi = shard_bounds(x.shape[0], world, rank)
     return x[lo:hi]
+
+
+_SYMM = {}  # (M, N, dtype, device index, group name) -> (buffer, handle)
+
+
+def _symmetric_output(M, N, dtype, device, group):
+    """A row-major [M, N] buffer allocated on every rank of `group` with the
+    other ranks' copies mapped into this process (torch symmetric memory,
+    CUDA backend: plain peer mappings, no NVSHMEM).  Cached per shape."""
+    import torch.distributed._symmetric_memory as symm_mem
+
+    pg = group if group is not None else dist.group.WORLD
+    key = (M, N, dtype, device.index, pg.group_name)
+    hit = _SYMM.get(key)
+    if hit is None:
+        if symm_mem.get_backend(device) is None:
+            symm_mem.set_backend("CUDA")
+        buf = symm_mem.empty(M, N, dtype=dtype, device=device)
+        hdl = symm_mem.rendezvous(buf, pg)
+        hit = _SYMM[key] = (buf, hdl)
+    return hit
+
+
+def nshard_mm_fused(a: torch.Tensor, b_shard: torch.Tensor, *, out_dtype=torch.float16, chunked: bool = True,
+                    group=None) -> torch.Tensor:
+    """C = A @ B with B column-sharded, gathered by the GEMM itself.
+
+    One kernel per rank computes its [M, N/P] panel and, tile by tile as the
+    product runs, stores every finished tile both into its own full [M, N]
+    output and into every other rank's (peer memory over NVLink,
+    `f16acc_gemm_allgather`); a device-side barrier across the ranks then
+    makes the gathered C complete everywhere.  Returns this rank's full
+    row-major C.  The buffer is reused across calls with the same shape:
+    consume (or copy) it before the next call.
+    """
+    from . import _lib
+    from .kernel import _OUT_CODES, _check, _raise, workspace_bytes
+
+    _check(a, b_shard)
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    M, K = a.shape
+    n_local = b_shard.shape[1]
+    N = world * n_local
+    buf, hdl = _symmetric_output(M, N, out_dtype, a.device, group)
+    esize = buf.element_size()
+    order = [rank] + [r for r in range(world) if r != rank]  # own block first
+    ptrs = [hdl.buffer_ptrs[r] + rank * n_local * esize for r in order]
+    outs = (ctypes.c_void_p * world)(*ptrs)
+    ws = torch.empty(workspace_bytes(M, n_local, K), dtype=torch.uint8, device=a.device) if chunked else None
+    lib = _lib.load()
+    hdl.barrier()  # no rank still reads its buffer from the previous call when the stores start
+    rc = lib.f16acc_gemm_allgather(a.data_ptr(), a.stride(0), a.stride(1), b_shard.data_ptr(), b_shard.stride(0),
+                                   b_shard.stride(1), outs, world, N, 1, _OUT_CODES[out_dtype], M, n_local, K,
+                                   1 if chunked else 0, ws.data_ptr() if ws is not None else None,
+                                   ws.numel() if ws is not None else 0, a.device.index,
+                                   torch.cuda.current_stream(a.device).cuda_stream)
+    if rc != _lib.OK:
+        _raise(rc)
+    hdl.barrier()  # every rank's tiles have landed in every buffer
+    return buf
 
 
 def _default_mm(a, b, out_dtype):

@@ -110,6 +110,23 @@ int f16acc_gemm_redo(const void *A, int64_t sAm, int64_t sAk,
                      void *workspace, size_t ws_bytes, int device, void *stream,
                      int variant);
 
+/* Fused GEMM + all-gather for an N-column-sharded product (no reference
+ * counterpart; the reference is single-GPU).  This rank computes
+ * A[M,K] @ B_shard[K,N] and stores every finished tile into n_outs output
+ * blocks with identical strides: outs[0] is this GPU's block, outs[1..] are
+ * the same block inside other GPUs' output buffers, mapped into this process
+ * (peer memory written over NVLink by plain stores, tile by tile while the
+ * product runs).  Typically each rank's outs[i] points at column offset
+ * rank * N of rank i's full [M, world * N] row-major C.  Chunked mode's redo
+ * pass rewrites its tiles in every output.  tcgen05 operands only (else
+ * F16ACC_ERR_UNSUPPORTED); n_outs <= 8.  The caller synchronises the ranks
+ * (a barrier after the call on each) before reading the gathered C. */
+int f16acc_gemm_allgather(const void *A, int64_t sAm, int64_t sAk,
+                          const void *B, int64_t sBk, int64_t sBn,
+                          void *const *outs, int n_outs, int64_t sCm, int64_t sCn, int c_dtype,
+                          int64_t M, int64_t N, int64_t K, int chunked,
+                          void *workspace, size_t ws_bytes, int device, void *stream);
+
 /* What f16acc_gemm_ex would run for these operands, without launching:
  * variant (F16ACC_VARIANT_TCGEN05 or _MMA_SYNC), output tile shape, and the
  * tile grid (flag slot of tile (tm, tn) = tm * tiles_n + tn, each slot
