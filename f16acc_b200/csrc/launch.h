@@ -19,8 +19,6 @@ struct TcShape {
     int bn;
     int epi_split;
 };
-int tc_threads(TcShape shape);
-int tc_smem_bytes(TcShape shape);
 bool tc_shape_supported(TcShape shape);
 cudaError_t launch_tc(const TcParams& p, TcShape shape, bool chunked, bool b_mn, int out, bool redo, int grid,
                       cudaStream_t stream);

@@ -53,7 +53,7 @@ struct TcParams {
     void* peers[kMaxPeers];
 };
 
-template <int BN_, int EPI_SPLIT_>
+template <int BN_, int EPI_SPLIT_, int OUT_>
 struct TcConfig {
     static constexpr int BM = 128;
     static constexpr int BN = BN_;
@@ -65,24 +65,65 @@ struct TcConfig {
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (BN == 256) ? 4 : 6;
+    static constexpr int OUT_BYTES = OUT_ == kOutF32 ? 4 : 2;
+    // Output staging: the finished tile is assembled in smem so rows leave in
+    // whole, coalesced 16-byte-per-lane stores (local C and every peer).  Row
+    // pitch padded by 16 bytes so the per-thread row writes spread over banks.
+    static constexpr int STAGE_PITCH = BN * OUT_BYTES + 16;
+    static constexpr int STAGING_BYTES = BM * STAGE_PITCH;
+    static constexpr int STAGES = OUT_BYTES == 4 ? 4 : 5;
     static constexpr int TMEM_COLS = 512;
     static constexpr int ACC_COLS = BN;  // one 32-bit TMEM column per accumulator element, f16 or f32
     static constexpr int NBUF = TMEM_COLS / ACC_COLS;
     static constexpr int BAR_BYTES = 256;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*alignment slack*/ + BAR_BYTES;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*alignment slack*/ + BAR_BYTES;
     static constexpr int FLAG_BYTES_PER_WARP = kFlagBytesPerTile / EPI_WARPS;  // every slot byte gets written
     static_assert(FLAG_BYTES_PER_WARP * EPI_WARPS == kFlagBytesPerTile &&
                       (FLAG_BYTES_PER_WARP == 1 || FLAG_BYTES_PER_WARP == 2),
                   "flag slot split over the epilogue warps");
     static_assert(CW == 32 || CW % 64 == 0, "epilogue column slice");
-    static_assert((2 * STAGES + 2 * NBUF + 1) * 8 + 16 <= BAR_BYTES, "barrier area");
+    static_assert((2 * STAGES + 2 * NBUF + 2) * 8 + 16 <= BAR_BYTES, "barrier area");
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 };
 
+// Write this thread's CW accumulators of one tile row into the smem staging tile.
+template <int OUT, int CW, int PITCH>
+__device__ __forceinline__ void stage_row(uint8_t* staging, int row_in_tile, int col_in_tile, const float (&acc)[CW]) {
+    using Tr = OutTraits<OUT>;
+    uint8_t* dst = staging + row_in_tile * PITCH + col_in_tile * int(sizeof(typename Tr::T));
+#pragma unroll
+    for (int j = 0; j < CW; j += Tr::kVec) *reinterpret_cast<uint4*>(dst + j * int(sizeof(typename Tr::T))) = pack16<OUT>(&acc[j]);
+}
+
+// Copy the staged BM x BN tile to `n_dst` outputs with identical row stride:
+// lanes run along a row, 16 bytes each, so every store instruction writes
+// whole contiguous row segments.  Column tails past N go element by element.
+template <int OUT, int BM, int BN, int PITCH, int NWARPS>
+__device__ __forceinline__ void store_staged(const uint8_t* staging, void* const* dst, int n_dst, int64_t sCm,
+                                             int row0, int col0, int M, int N, int warp_idx, int lane) {
+    using Tr = OutTraits<OUT>;
+    using T = typename Tr::T;
+    constexpr int kChunks = BN * int(sizeof(T)) / 16;  // 16-byte pieces per tile row
+    for (int idx = warp_idx * 32 + lane; idx < BM * kChunks; idx += NWARPS * 32) {
+        const int r = idx / kChunks, c16 = idx - r * kChunks;
+        const int grow = row0 + r, gcol = col0 + c16 * Tr::kVec;
+        if (grow >= M || gcol >= N) continue;
+        const uint4 v = *reinterpret_cast<const uint4*>(staging + r * PITCH + c16 * 16);
+        const int64_t off = int64_t(grow) * sCm + gcol;
+        if (gcol + Tr::kVec <= N) {
+            for (int d = 0; d < n_dst; ++d) *reinterpret_cast<uint4*>(reinterpret_cast<T*>(dst[d]) + off) = v;
+        } else {
+            const T* e = reinterpret_cast<const T*>(&v);
+            for (int d = 0; d < n_dst; ++d)
+                for (int t = 0; t < Tr::kVec && gcol + t < N; ++t) reinterpret_cast<T*>(dst[d])[off + t] = e[t];
+        }
+    }
+}
+
 template <int BN, int EPI_SPLIT, bool CHUNKED, bool B_MN, int OUT, bool REDO>
-__global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT>::THREADS, 1)
+__global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ TcParams p) {
-    using Cfg = TcConfig<BN, EPI_SPLIT>;
+    using Cfg = TcConfig<BN, EPI_SPLIT, OUT>;
     constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES, NBUF = Cfg::NBUF, CW = Cfg::CW;
     static_assert(!(CHUNKED && REDO), "the redo pass runs in FP32 mode");
 
@@ -90,12 +131,14 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT>::THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+    uint8_t* staging = smem + STAGES * Cfg::STAGE_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + Cfg::STAGING_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + NBUF;
     uint64_t* drain = tempty + NBUF;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* epi_bar = drain + 1;  // epilogue warps meet here around the staged store
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -111,6 +154,7 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT>::THREADS, 1)
             mbar_init(&tempty[b], Cfg::EPI_WARPS);
         }
         mbar_init(drain, 1);
+        mbar_init(epi_bar, Cfg::EPI_WARPS);
         *abort_flag = 0;
         fence_mbarrier_init();
         tma_prefetch_desc(&p.tmA);
@@ -240,6 +284,9 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT>::THREADS, 1)
         const int q = warp & 3;          // TMEM lane quarter this warp may access
         const int colg = e >> 2;         // column slice
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+        void* dsts[1 + kMaxPeers] = {p.C};  // this GPU's C, then the peers' copies
+        for (int i = 0; i < p.n_peers; ++i) dsts[1 + i] = p.peers[i];
+        uint32_t epi_phase = 0;
         ChunkRing<NBUF> ring{tfull, tempty, tmem + lane_base + colg * CW, Cfg::ACC_COLS};    // FP32 mode
         PairRing<CW> pairs{tfull, tempty, tmem + lane_base + colg * CW, Cfg::ACC_COLS};     // chunked mode
         for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
@@ -276,12 +323,30 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT>::THREADS, 1)
                 }
                 ring.release(lane);
             }
-            const int row = tm * BM + q * 32 + lane;
-            const int col0 = tn * BN + colg * CW;
-            store_row<OUT, CW>(p.C, p.sCm, p.sCn, row, col0, p.M, p.N, acc, p.c_vec != 0);
-            // fused all-gather: the same tile into every peer's buffer, over NVLink
-            for (int i = 0; i < p.n_peers; ++i)
-                store_row<OUT, CW>(p.peers[i], p.sCm, p.sCn, row, col0, p.M, p.N, acc, p.c_vec != 0);
+            if (p.c_vec) {
+                // Stage the tile in smem, then write whole rows to C and to every peer's
+                // buffer (fused all-gather): coalesced 16-byte-per-lane stores.
+                stage_row<OUT, CW, Cfg::STAGE_PITCH>(staging, q * 32 + lane, colg * CW, acc);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(epi_bar);
+                if (!__all_sync(0xffffffffu, mbar_wait(epi_bar, epi_phase, abort_flag, p.status,
+                                                        kStatusTimeoutEpilogue)))
+                    break;
+                epi_phase ^= 1u;
+                store_staged<OUT, BM, BN, Cfg::STAGE_PITCH, Cfg::EPI_WARPS>(staging, dsts, 1 + p.n_peers, p.sCm,
+                                                                            tm * BM, tn * BN, p.M, p.N, e, lane);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(epi_bar);  // staging free again once every warp has copied out
+                if (!__all_sync(0xffffffffu, mbar_wait(epi_bar, epi_phase, abort_flag, p.status,
+                                                        kStatusTimeoutEpilogue)))
+                    break;
+                epi_phase ^= 1u;
+            } else {
+                const int row = tm * BM + q * 32 + lane;
+                const int col0 = tn * BN + colg * CW;
+                for (int d = 0; d <= p.n_peers; ++d)
+                    store_row<OUT, CW>(dsts[d], p.sCm, p.sCn, row, col0, p.M, p.N, acc, false);
+            }
         }
         // peer stores become visible system-wide before the kernel is seen complete
         if (p.n_peers > 0) __threadfence_system();

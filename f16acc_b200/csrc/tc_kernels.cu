@@ -29,7 +29,7 @@ cudaError_t ensure_smem_attr(Kernel kernel, int smem) {
 
 template <int BN, int EPI, bool CHUNKED, bool B_MN, int OUT, bool REDO>
 cudaError_t launch_one(const TcParams& p, int grid, cudaStream_t stream) {
-    using Cfg = TcConfig<BN, EPI>;
+    using Cfg = TcConfig<BN, EPI, OUT>;
     auto kernel = tc_gemm_kernel<BN, EPI, CHUNKED, B_MN, OUT, REDO>;
     cudaError_t e = ensure_smem_attr(kernel, Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return e;
@@ -64,18 +64,6 @@ cudaError_t launch_shape(const TcParams& p, bool chunked, bool b_mn, int out, bo
 }  // namespace
 
 bool tc_shape_supported(TcShape s) { return s.bn == 128 && (s.epi_split == 2 || s.epi_split == 4); }
-
-int tc_threads(TcShape s) {
-    if (s.bn == 128 && s.epi_split == 2) return TcConfig<128, 2>::THREADS;
-    if (s.bn == 128 && s.epi_split == 4) return TcConfig<128, 4>::THREADS;
-    return 0;
-}
-
-int tc_smem_bytes(TcShape s) {
-    if (s.bn == 128 && s.epi_split == 2) return TcConfig<128, 2>::SMEM_BYTES;
-    if (s.bn == 128 && s.epi_split == 4) return TcConfig<128, 4>::SMEM_BYTES;
-    return 0;
-}
 
 cudaError_t launch_tc(const TcParams& p, TcShape shape, bool chunked, bool b_mn, int out, bool redo, int grid,
                       cudaStream_t stream) {
