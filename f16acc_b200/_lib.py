@@ -32,6 +32,7 @@ SIGNATURES = {
     "f16acc_gemm_ex": (_int, _GEMM_ARGS + [_int]),
     "f16acc_gemm_main": (_int, _GEMM_ARGS + [_int]),
     "f16acc_gemm_redo": (_int, _GEMM_ARGS + [_int]),
+    "f16acc_gemm_bias": (_int, _GEMM_ARGS[:6] + [_p, _i64] + _GEMM_ARGS[6:] + [_int]),
     "f16acc_gemm_allgather": (_int, [_p, _i64, _i64, _p, _i64, _i64, ctypes.POINTER(ctypes.c_void_p), _int, _i64, _i64,
                                      _int, _i64, _i64, _i64, _int, _p, _size, _int, _p]),
     "f16acc_workspace_bytes": (_size, [_i64, _i64, _i64]),

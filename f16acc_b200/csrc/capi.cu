@@ -161,7 +161,8 @@ struct DeviceGuard {
 
 int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int64_t sBn, void* C, int64_t sCm,
         int64_t sCn, int c_dtype, int64_t M, int64_t N, int64_t K, int chunked, void* workspace, size_t ws_bytes,
-        int device, void* stream_ptr, int variant, int phases, void* const* peers = nullptr, int n_peers = 0) {
+        int device, void* stream_ptr, int variant, int phases, void* const* peers = nullptr, int n_peers = 0,
+        const void* bias = nullptr, int64_t sbias = 0) {
     if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && peers == nullptr)) return F16ACC_ERR_INVALID_ARGUMENT;
     for (int i = 0; i < n_peers; ++i)
         if (peers[i] == nullptr) return F16ACC_ERR_INVALID_ARGUMENT;
@@ -180,8 +181,10 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
 
     if (K == 0) {  // empty sum: C = 0, nothing to flag
         if (!(phases & kPhaseMain)) return F16ACC_OK;
-        return launch_fill_zero(C, sCm, sCn, int(M), int(N), c_dtype, stream) == cudaSuccess ? F16ACC_OK
-                                                                                             : F16ACC_ERR_CUDA;
+        return launch_fill_zero(C, sCm, sCn, int(M), int(N), c_dtype, stream, static_cast<const __half*>(bias),
+                                sbias) == cudaSuccess
+                   ? F16ACC_OK
+                   : F16ACC_ERR_CUDA;
     }
     if (A == nullptr || B == nullptr) return F16ACC_ERR_INVALID_ARGUMENT;
     const Layout L = analyse(A, sAm, sAk, B, sBk, sBn, M, N, K);
@@ -228,6 +231,8 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
         p.status = info->status;
         p.n_peers = n_peers;
         for (int i = 0; i < n_peers; ++i) p.peers[i] = peers[i];
+        p.bias = static_cast<const __half*>(bias);
+        p.sbias = sbias;
         const int64_t tiles = int64_t(p.tiles_m) * p.tiles_n;
         const int sms = usable_sms(info->sms);
         const int grid = int(tiles < sms ? tiles : sms);
@@ -260,6 +265,8 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
     q.group_m = kGroupM;
     q.c_vec = (sCn == 1 && pc % (2 * esize) == 0 && sCm % 2 == 0) ? 1 : 0;
     q.flags = static_cast<uint8_t*>(workspace);
+    q.bias = static_cast<const __half*>(bias);
+    q.sbias = sbias;
     const int a_mode = L.a_vec ? kLoadKVec : kLoadGeneric;
     const int b_mode = L.b_kvec ? kLoadKVec : (L.b_nvec ? kLoadNVec : kLoadGeneric);
     const int64_t tiles = int64_t(q.tiles_m) * q.tiles_n;
@@ -319,6 +326,15 @@ int f16acc_gemm_allgather(const void* A, int64_t sAm, int64_t sAk, const void* B
                stream, F16ACC_VARIANT_TCGEN05, kPhaseBoth, outs + 1, n_outs - 1);
 }
 
+int f16acc_gemm_bias(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int64_t sBn,
+                     const void* bias, int64_t sbias, void* C, int64_t sCm, int64_t sCn, int c_dtype, int64_t M,
+                     int64_t N, int64_t K, int chunked, void* workspace, size_t ws_bytes, int device, void* stream,
+                     int variant) {
+    if (bias == nullptr && M > 0 && N > 0) return F16ACC_ERR_INVALID_ARGUMENT;
+    return run(A, sAm, sAk, B, sBk, sBn, C, sCm, sCn, c_dtype, M, N, K, chunked, workspace, ws_bytes, device, stream,
+               variant, kPhaseBoth, nullptr, 0, bias, sbias);
+}
+
 size_t f16acc_workspace_bytes(int64_t M, int64_t N, int64_t K) {
     (void)K;
     if (M <= 0 || N <= 0) return 16;
@@ -361,7 +377,7 @@ int f16acc_flag_bytes_per_tile(void) { return kFlagBytesPerTile; }
 
 int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void* out, int device, void* stream) {
     const bool known = (mode >= 0 && mode <= 15 && mode != 5) || (mode >= 20 && mode <= 28) ||
-                       (mode >= 30 && mode <= 36) || (mode >= 40 && mode <= 43) || mode == 45;
+                       (mode >= 30 && mode <= 36) || (mode >= 40 && mode <= 43) || mode == 45 || mode == 46;
     if (!known || chunks < 0 || grid <= 0 || out == nullptr) return F16ACC_ERR_INVALID_ARGUMENT;
     if (mode >= 2 && mode < 30 && epi_split != 2 && epi_split != 4) return F16ACC_ERR_INVALID_ARGUMENT;
     DeviceInfo* info = device_info(device);

@@ -47,19 +47,34 @@ struct OutTraits<kOutF16> {
     using T = __half;
     static constexpr int kVec = 8;  // elements per 16-byte store
     __device__ static T cvt(float x) { return __float2half_rn(x); }
+    __device__ static float round_trip(float x) { return __half2float(__float2half_rn(x)); }
+    __device__ static float to_float(T x) { return __half2float(x); }
 };
 template <>
 struct OutTraits<kOutBF16> {
     using T = __nv_bfloat16;
     static constexpr int kVec = 8;
     __device__ static T cvt(float x) { return __float2bfloat16_rn(x); }
+    __device__ static float round_trip(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+    __device__ static float to_float(T x) { return __bfloat162float(x); }
 };
 template <>
 struct OutTraits<kOutF32> {
     using T = float;
     static constexpr int kVec = 4;
     __device__ static T cvt(float x) { return x; }
+    __device__ static float round_trip(float x) { return x; }
+    __device__ static float to_float(T x) { return x; }
 };
+
+// Bias epilogue: the product is rounded to the output type first and the bias
+// added to that value, so C = cvt(cvt(A@B) + bias) is bit-identical to the
+// reference's unfused `y = mm(x, w.t()); y += b` (patch.py:28-30), whose
+// in-place half add computes in FP32 and rounds once.
+template <int OUT>
+__device__ __forceinline__ float add_bias(float acc, const __half* bias, int64_t sbias, int col) {
+    return OutTraits<OUT>::round_trip(acc) + __half2float(bias[int64_t(col) * sbias]);
+}
 
 // 16 bytes of output built from kVec consecutive accumulators.
 template <int OUT>
@@ -88,29 +103,31 @@ __device__ __forceinline__ uint4 pack16(const float* v) {
     return u;
 }
 
-// Store CW consecutive accumulators of one output row, columns [col0, col0+CW).
-// `vec` = C has unit column stride and 16-byte aligned rows, so full 16-byte
-// groups go out as vector stores; everything else is element by element with
-// bounds checks.  64-bit offsets throughout (outputs past 2^31 elements).
-template <int OUT, int CW>
-__device__ __forceinline__ void store_row(void* C, int64_t sCm, int64_t sCn, int row, int col0, int M, int N,
-                                          const float (&acc)[CW], bool vec) {
-    using Tr = OutTraits<OUT>;
-    using T = typename Tr::T;
-    if (row >= M) return;
-    T* crow = reinterpret_cast<T*>(C) + static_cast<int64_t>(row) * sCm;
-    if (vec && col0 + CW <= N) {
+// add_bias over 16 bytes of output already rounded to OUT (columns col ..
+// col + kVec - 1; the ones at or past N are left as they are).
+template <int OUT>
+__device__ __forceinline__ uint4 add_bias16(uint4 u, const __half* bias, int64_t sbias, int col, int N) {
+    constexpr int kVec = OutTraits<OUT>::kVec;
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    float f[kVec];
 #pragma unroll
-        for (int j = 0; j < CW; j += Tr::kVec) {
-            *reinterpret_cast<uint4*>(crow + col0 + j) = pack16<OUT>(&acc[j]);
+    for (int i = 0; i < 4; ++i) {
+        if constexpr (OUT == kOutF32) {
+            f[i] = __uint_as_float(w[i]);
+        } else if constexpr (OUT == kOutF16) {
+            const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            f[2 * i] = t.x;
+            f[2 * i + 1] = t.y;
+        } else {
+            const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+            f[2 * i] = t.x;
+            f[2 * i + 1] = t.y;
         }
-        return;
     }
 #pragma unroll
-    for (int j = 0; j < CW; ++j) {
-        const int col = col0 + j;
-        if (col < N) crow[static_cast<int64_t>(col) * sCn] = Tr::cvt(acc[j]);
-    }
+    for (int t = 0; t < kVec; ++t)
+        if (col + t < N) f[t] += __half2float(bias[int64_t(col + t) * sbias]);
+    return pack16<OUT>(f);
 }
 
 }  // namespace f16acc

@@ -26,7 +26,9 @@ cudaError_t launch_tc(const TcParams& p, TcShape shape, bool chunked, bool b_mn,
 // mma.sync kernel: a_mode / b_mode from LoadMode.
 cudaError_t launch_mma(const MmaParams& p, bool chunked, int a_mode, int b_mode, int out, bool redo, int grid,
                        cudaStream_t stream);
-cudaError_t launch_fill_zero(void* C, int64_t sCm, int64_t sCn, int M, int N, int out, cudaStream_t stream);
+// K = 0: C = 0, or C[r][c] = bias[c] when a bias is given.
+cudaError_t launch_fill_zero(void* C, int64_t sCm, int64_t sCn, int M, int N, int out, cudaStream_t stream,
+                             const __half* bias = nullptr, int64_t sbias = 0);
 
 // Raw-rate probe (probes.cu): mode 0/1 MMA only with FP16/FP32 accumulator,
 // mode 2 the chunk pipeline; `out` holds grid * (64 + 128 * epi_split) floats.

@@ -30,6 +30,8 @@ struct MmaParams {
     int group_m;
     int c_vec;  // C has unit column stride and 4-byte aligned pairs
     uint8_t* flags;
+    const __half* bias;  // optional per-column bias (element stride sbias), added before the cast
+    int64_t sbias;
 };
 
 // Operand load modes.
@@ -240,6 +242,26 @@ __global__ void __launch_bounds__(MmaCfg::THREADS) mma_gemm_kernel(const __grid_
             if (lane == 0) *reinterpret_cast<uint16_t*>(p.flags + tile_id * kFlagBytesPerTile + 2 * warp) = bad ? 1 : 0;
         }
 
+        if (p.bias != nullptr) {  // after the flag, as the reference adds it outside the kernel
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int col = tn * BN + wn * 32 + j * 8 + 2 * tq;
+                if (col < p.N) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        acc[i][j][0] = add_bias<OUT>(acc[i][j][0], p.bias, p.sbias, col);
+                        acc[i][j][2] = add_bias<OUT>(acc[i][j][2], p.bias, p.sbias, col);
+                    }
+                }
+                if (col + 1 < p.N) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        acc[i][j][1] = add_bias<OUT>(acc[i][j][1], p.bias, p.sbias, col + 1);
+                        acc[i][j][3] = add_bias<OUT>(acc[i][j][3], p.bias, p.sbias, col + 1);
+                    }
+                }
+            }
+        }
         // Store: acc[i][j] = rows r0 (v 0,1) and r0+8 (v 2,3), columns c, c+1.
         using Tr = OutTraits<OUT>;
         using T = typename Tr::T;
@@ -273,15 +295,16 @@ __global__ void __launch_bounds__(MmaCfg::THREADS) mma_gemm_kernel(const __grid_
     }
 }
 
-// C = 0 for K == 0 (an empty sum), any strides.
+// C = 0 (or the bias broadcast over rows) for K == 0, an empty sum; any strides.
 template <int OUT>
-__global__ void fill_zero_kernel(void* C, int64_t sCm, int64_t sCn, int M, int N) {
+__global__ void fill_zero_kernel(void* C, int64_t sCm, int64_t sCn, int M, int N, const __half* bias, int64_t sbias) {
     using T = typename OutTraits<OUT>::T;
     T* c = reinterpret_cast<T*>(C);
     const int64_t total = int64_t(M) * N;
     for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
         const int64_t r = i / N, col = i - r * N;
-        c[r * sCm + col * sCn] = OutTraits<OUT>::cvt(0.0f);
+        const float v = bias != nullptr ? __half2float(bias[col * sbias]) : 0.0f;  // K = 0: empty sum, plus the bias
+        c[r * sCm + col * sCn] = OutTraits<OUT>::cvt(v);
     }
 }
 

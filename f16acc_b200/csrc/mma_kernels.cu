@@ -49,14 +49,17 @@ cudaError_t launch_mma(const MmaParams& p, bool chunked, int a_mode, int b_mode,
     return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_fill_zero(void* C, int64_t sCm, int64_t sCn, int M, int N, int out, cudaStream_t stream) {
+cudaError_t launch_fill_zero(void* C, int64_t sCm, int64_t sCn, int M, int N, int out, cudaStream_t stream,
+                             const __half* bias, int64_t sbias) {
     const int64_t total = int64_t(M) * N;
     const int threads = 256;
     const int grid = static_cast<int>(total / threads + 1 < 4096 ? total / threads + 1 : 4096);
     switch (out) {
-        case kOutF16: fill_zero_kernel<kOutF16><<<grid, threads, 0, stream>>>(C, sCm, sCn, M, N); break;
-        case kOutF32: fill_zero_kernel<kOutF32><<<grid, threads, 0, stream>>>(C, sCm, sCn, M, N); break;
-        case kOutBF16: fill_zero_kernel<kOutBF16><<<grid, threads, 0, stream>>>(C, sCm, sCn, M, N); break;
+        case kOutF16: fill_zero_kernel<kOutF16><<<grid, threads, 0, stream>>>(C, sCm, sCn, M, N, bias, sbias); break;
+        case kOutF32: fill_zero_kernel<kOutF32><<<grid, threads, 0, stream>>>(C, sCm, sCn, M, N, bias, sbias); break;
+        case kOutBF16:
+            fill_zero_kernel<kOutBF16><<<grid, threads, 0, stream>>>(C, sCm, sCn, M, N, bias, sbias);
+            break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(64 + 128 * EPI_SPLIT, 1) chunk_rate_kernel(int
         for (int b = 0; b < NBUF; ++b) {
             mbar_init(&tfull[b], 1);
             // mode 41: only the 8 warps that own a chunk (2 column slices x 4 quarters) release it
-            mbar_init(&tempty[b], MODE == 41 ? 8 : (ProbeMode<MODE>::PER_THREAD ? 32 : 1) * 4 * EPI_SPLIT);
+            mbar_init(&tempty[b], (MODE == 41 || MODE == 46) ? 8 : (ProbeMode<MODE>::PER_THREAD ? 32 : 1) * 4 * EPI_SPLIT);
         }
         mbar_init(done, 1);
         *abort_flag = 0;
@@ -91,6 +91,59 @@ __global__ void __launch_bounds__(64 + 128 * EPI_SPLIT, 1) chunk_rate_kernel(int
             if (!mbar_wait_drain(done, ph)) break;
             ph ^= 1u;
         }
+    } else if (MODE == 46 && warp == 1 && lane == 0) {
+        // pairs split by N-halves: per pair and half, 4 MMAs N=64 (2 chunks) + one commit;
+        // tfull/tempty index = half * 2 + pair
+        constexpr uint32_t idesc = idesc_f16(false, false, BM, 64);
+        uint32_t p = 0, ph = 0;
+        for (int c = 0; c < chunks; c += 2) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (!mbar_wait(&tempty[h * 2 + p], ph ^ 1u, abort_flag, status, kStatusTimeoutProbe)) goto probe46_done;
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < 2; ++k)
+#pragma unroll
+                    for (int s = 0; s < 2; ++s)
+                        umma_f16(tmem + (2 * p + k) * BN + h * 64, sdesc_sw128(a0 + s * 32, 16, 1024),
+                                 sdesc_sw128(b0 + h * 64 * 128 + s * 32, 16, 1024), idesc, s);
+                umma_commit(&tfull[h * 2 + p]);
+            }
+            p ^= 1u;
+            if (p == 0) ph ^= 1u;
+        }
+    probe46_done:
+        umma_commit(done);
+        mbar_wait_drain(done, 0);
+    } else if (MODE == 46 && warp >= 2) {
+        const int e = warp - 2, q = warp & 3, colg = e >> 2, half = colg >> 1;  // 16 warps, 32 columns each
+        const uint32_t base = tmem + (static_cast<uint32_t>(q * 32) << 16) + colg * 32;
+        float acc[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
+        uint32_t p = 0, ph = 0;
+        for (int c = 0; c < chunks; c += 2) {
+            const bool ok = mbar_wait(&tfull[half * 2 + p], ph, abort_flag, status, kStatusTimeoutProbe);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            uint32_t r0[16], r1[16];
+            tmem_ld_chunk<32>(base + (2 * p) * BN, r0);
+            tmem_ld_chunk<32>(base + (2 * p + 1) * BN, r1);
+            tmem_wait_ld();
+            reg_fence(r0);
+            reg_fence(r1);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[half * 2 + p]);
+            add_chunk<32>(acc, r0);
+            add_chunk<32>(acc, r1);
+            p ^= 1u;
+            if (p == 0) ph ^= 1u;
+        }
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) s += acc[j];
+        out[blockIdx.x * blockDim.x + threadIdx.x] = s;
     } else if (MODE == 45 && warp == 1 && lane == 0) {
         // wide chunks: 2 MMAs N=256 per chunk into 2 buffers of 256 columns
         constexpr uint32_t idesc = idesc_f16(false, false, BM, 256);
@@ -622,6 +675,7 @@ cudaError_t launch_chunk_rate(int mode, int epi_split, int chunks, int grid, flo
             case 42: return launch_probe<42, 4>(chunks, grid, out, status, stream);
             case 43: return launch_probe<43, 4>(chunks, grid, out, status, stream);
             case 45: return launch_probe<45, 4>(chunks, grid, out, status, stream);
+            case 46: return launch_probe<46, 4>(chunks, grid, out, status, stream);
         }
     }
     return cudaErrorInvalidValue;

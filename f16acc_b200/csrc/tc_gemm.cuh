@@ -51,6 +51,10 @@ struct TcParams {
     // plain GEMM.
     int n_peers;
     void* peers[kMaxPeers];
+    // Optional bias, one fp16 value per output column (element stride sbias),
+    // added to the FP32 result before the cast (nn.Linear's y = x W^T + b).
+    const __half* bias;
+    int64_t sbias;
 };
 
 template <int BN_, int EPI_SPLIT_, int OUT_>
@@ -100,7 +104,8 @@ __device__ __forceinline__ void stage_row(uint8_t* staging, int row_in_tile, int
 // whole contiguous row segments.  Column tails past N go element by element.
 template <int OUT, int BM, int BN, int PITCH, int NWARPS>
 __device__ __forceinline__ void store_staged(const uint8_t* staging, void* const* dst, int n_dst, int64_t sCm,
-                                             int row0, int col0, int M, int N, int warp_idx, int lane) {
+                                             int row0, int col0, int M, int N, int warp_idx, int lane,
+                                             const __half* bias, int64_t sbias) {
     using Tr = OutTraits<OUT>;
     using T = typename Tr::T;
     constexpr int kChunks = BN * int(sizeof(T)) / 16;  // 16-byte pieces per tile row
@@ -108,7 +113,8 @@ __device__ __forceinline__ void store_staged(const uint8_t* staging, void* const
         const int r = idx / kChunks, c16 = idx - r * kChunks;
         const int grow = row0 + r, gcol = col0 + c16 * Tr::kVec;
         if (grow >= M || gcol >= N) continue;
-        const uint4 v = *reinterpret_cast<const uint4*>(staging + r * PITCH + c16 * 16);
+        uint4 v = *reinterpret_cast<const uint4*>(staging + r * PITCH + c16 * 16);
+        if (bias != nullptr) v = add_bias16<OUT>(v, bias, sbias, gcol, N);
         const int64_t off = int64_t(grow) * sCm + gcol;
         if (gcol + Tr::kVec <= N) {
             for (int d = 0; d < n_dst; ++d) *reinterpret_cast<uint4*>(reinterpret_cast<T*>(dst[d]) + off) = v;
@@ -117,6 +123,28 @@ __device__ __forceinline__ void store_staged(const uint8_t* staging, void* const
             for (int d = 0; d < n_dst; ++d)
                 for (int t = 0; t < Tr::kVec && gcol + t < N; ++t) reinterpret_cast<T*>(dst[d])[off + t] = e[t];
         }
+    }
+}
+
+// The same copy-out for outputs of any strides, one element per lane: lanes
+// run along a row when columns are contiguous (sCn == 1), else down a column,
+// which is the contiguous direction of a transposed C.
+template <int OUT, int BM, int BN, int PITCH, int NWARPS>
+__device__ __forceinline__ void store_staged_strided(const uint8_t* staging, void* const* dst, int n_dst, int64_t sCm,
+                                                     int64_t sCn, int row0, int col0, int M, int N, int warp_idx,
+                                                     int lane, const __half* bias, int64_t sbias) {
+    using Tr = OutTraits<OUT>;
+    using T = typename Tr::T;
+    const bool along_row = sCn == 1;
+    for (int idx = warp_idx * 32 + lane; idx < BM * BN; idx += NWARPS * 32) {
+        const int r = along_row ? idx / BN : idx % BM;
+        const int c = along_row ? idx % BN : idx / BM;
+        const int grow = row0 + r, gcol = col0 + c;
+        if (grow >= M || gcol >= N) continue;
+        T v = *reinterpret_cast<const T*>(staging + r * PITCH + c * int(sizeof(T)));
+        if (bias != nullptr) v = Tr::cvt(Tr::to_float(v) + __half2float(bias[int64_t(gcol) * sbias]));
+        const int64_t off = int64_t(grow) * sCm + int64_t(gcol) * sCn;
+        for (int d = 0; d < n_dst; ++d) reinterpret_cast<T*>(dst[d])[off] = v;
     }
 }
 
@@ -323,30 +351,31 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
                 }
                 ring.release(lane);
             }
-            if (p.c_vec) {
-                // Stage the tile in smem, then write whole rows to C and to every peer's
-                // buffer (fused all-gather): coalesced 16-byte-per-lane stores.
-                stage_row<OUT, CW, Cfg::STAGE_PITCH>(staging, q * 32 + lane, colg * CW, acc);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(epi_bar);
-                if (!__all_sync(0xffffffffu, mbar_wait(epi_bar, epi_phase, abort_flag, p.status,
-                                                        kStatusTimeoutEpilogue)))
-                    break;
-                epi_phase ^= 1u;
-                store_staged<OUT, BM, BN, Cfg::STAGE_PITCH, Cfg::EPI_WARPS>(staging, dsts, 1 + p.n_peers, p.sCm,
-                                                                            tm * BM, tn * BN, p.M, p.N, e, lane);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(epi_bar);  // staging free again once every warp has copied out
-                if (!__all_sync(0xffffffffu, mbar_wait(epi_bar, epi_phase, abort_flag, p.status,
-                                                        kStatusTimeoutEpilogue)))
-                    break;
-                epi_phase ^= 1u;
-            } else {
-                const int row = tm * BM + q * 32 + lane;
-                const int col0 = tn * BN + colg * CW;
-                for (int d = 0; d <= p.n_peers; ++d)
-                    store_row<OUT, CW>(dsts[d], p.sCm, p.sCn, row, col0, p.M, p.N, acc, false);
-            }
+            // Stage the tile in smem (rounded to the output type), then copy it out to C
+            // and to every peer's buffer (fused all-gather): whole rows in coalesced
+            // 16-byte-per-lane stores when C allows, else element by element.  The bias
+            // (after the flag: the reference adds it outside the kernel) goes on in the
+            // copy-out, to the product already rounded to the output type.
+            stage_row<OUT, CW, Cfg::STAGE_PITCH>(staging, q * 32 + lane, colg * CW, acc);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(epi_bar);
+            if (!__all_sync(0xffffffffu,
+                            mbar_wait(epi_bar, epi_phase, abort_flag, p.status, kStatusTimeoutEpilogue)))
+                break;
+            epi_phase ^= 1u;
+            if (p.c_vec)
+                store_staged<OUT, BM, BN, Cfg::STAGE_PITCH, Cfg::EPI_WARPS>(
+                    staging, dsts, 1 + p.n_peers, p.sCm, tm * BM, tn * BN, p.M, p.N, e, lane, p.bias, p.sbias);
+            else
+                store_staged_strided<OUT, BM, BN, Cfg::STAGE_PITCH, Cfg::EPI_WARPS>(
+                    staging, dsts, 1 + p.n_peers, p.sCm, p.sCn, tm * BM, tn * BN, p.M, p.N, e, lane, p.bias,
+                    p.sbias);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(epi_bar);  // staging free again once every warp has copied out
+            if (!__all_sync(0xffffffffu,
+                            mbar_wait(epi_bar, epi_phase, abort_flag, p.status, kStatusTimeoutEpilogue)))
+                break;
+            epi_phase ^= 1u;
         }
         // peer stores become visible system-wide before the kernel is seen complete
         if (p.n_peers > 0) __threadfence_system();

@@ -43,11 +43,22 @@ def workspace_bytes(M: int, N: int, K: int) -> int:
     return int(_lib.load().f16acc_workspace_bytes(M, N, K))
 
 
-def mm_ex(a, b, out_dtype=torch.float16, chunked=True, *, variant=_lib.VARIANT_AUTO, out=None, workspace=None):
-    """`mm` with the kernel variant forced and optional caller-owned output and
-    workspace (tests and benchmarks read the per-tile flags from it).
+def _check_bias(bias, a, n):
+    if not (isinstance(bias, torch.Tensor) and bias.dtype == torch.float16 and bias.device == a.device):
+        raise ValueError("bias must be an fp16 tensor on the operands' device")
+    if bias.dim() != 1 or bias.shape[0] != n:
+        raise ValueError(f"bias must have shape ({n},), got {tuple(bias.shape)}")
+
+
+def mm_ex(a, b, out_dtype=torch.float16, chunked=True, *, variant=_lib.VARIANT_AUTO, out=None, workspace=None,
+          bias=None):
+    """`mm` with the kernel variant forced, optional caller-owned output and
+    workspace (tests and benchmarks read the per-tile flags from it), and an
+    optional fp16 bias[N] added in the epilogue (see `mm_bias`).
     Returns (c, workspace)."""
     _check(a, b)
+    if bias is not None:
+        _check_bias(bias, a, b.shape[1])
     code = _OUT_CODES.get(out_dtype)
     if code is None:
         raise ValueError(f"mm supports out_dtype float16, float32 or bfloat16, got {out_dtype}")
@@ -68,12 +79,27 @@ def mm_ex(a, b, out_dtype=torch.float16, chunked=True, *, variant=_lib.VARIANT_A
         ws_ptr, ws_len = workspace.data_ptr(), workspace.numel()
     dev = a.device.index if a.device.index is not None else torch.cuda.current_device()
     stream = torch.cuda.current_stream(a.device).cuda_stream
-    rc = lib.f16acc_gemm_ex(a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(), b.stride(0), b.stride(1),
-                            out.data_ptr(), out.stride(0), out.stride(1), code, M, N, K, 1 if chunked else 0,
-                            ws_ptr, ws_len, dev, stream, int(variant))
+    if bias is None:
+        rc = lib.f16acc_gemm_ex(a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(), b.stride(0), b.stride(1),
+                                out.data_ptr(), out.stride(0), out.stride(1), code, M, N, K, 1 if chunked else 0,
+                                ws_ptr, ws_len, dev, stream, int(variant))
+    else:
+        rc = lib.f16acc_gemm_bias(a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(), b.stride(0), b.stride(1),
+                                  bias.data_ptr(), bias.stride(0), out.data_ptr(), out.stride(0), out.stride(1),
+                                  code, M, N, K, 1 if chunked else 0, ws_ptr, ws_len, dev, stream, int(variant))
     if rc != _lib.OK:
         _raise(rc)
     return out, workspace
+
+
+def mm_bias(a, b, bias, out_dtype=torch.float16, chunked=True):
+    """C = a @ b + bias with the bias added in the GEMM's epilogue.
+
+    Bit-identical to the reference's `y = mm(a, b); y += bias`
+    (patch.py:28-30) for an fp16 `bias` of shape (N,): the product is rounded
+    to out_dtype, the bias added in FP32 and the sum rounded once more, without
+    the second pass over y."""
+    return mm_ex(a, b, out_dtype, chunked, bias=bias)[0]
 
 
 def mm(a, b, out_dtype=torch.float16, chunked=True):

@@ -7,13 +7,15 @@ F.linear is replaced (every nn.Linear calls it).  Inputs that are not fp16 on
 CUDA, need gradients, or have fewer than MIN_ROWS rows (token-by-token
 decode, memory bound) go to the original F.linear (cuBLAS).  FP16 chunk
 overflow is handled on the device (the tile is redone with FP32 accumulation),
-so there is no host sync per call.
+so there is no host sync per call.  An fp16 bias of shape (out_features,) is
+added inside the GEMM's epilogue instead of the reference's separate `y += b`
+pass (same bits); any other bias takes the reference's in-place add.
 """
 
 import torch
 import torch.nn.functional as F
 
-from .kernel import mm
+from .kernel import mm, mm_bias
 
 MIN_ROWS = 128
 _orig = F.linear
@@ -26,9 +28,14 @@ def linear(x, w, b=None):
         calls["original"] += 1
         return _orig(x, w, b)
     x2 = x.reshape(rows, x.shape[-1])
-    y = mm(x2, w.t())  # [K, N] view of the [N, K] weight: K-contiguous B, no copy
-    if b is not None:
-        y += b
+    n = w.shape[0]
+    if b is not None and b.dtype == torch.float16 and b.device == x.device and b.shape == (n,):
+        # Bias added in the GEMM epilogue; bit-identical to `y += b` after mm.
+        y = mm_bias(x2, w.t(), b)
+    else:
+        y = mm(x2, w.t())  # [K, N] view of the [N, K] weight: K-contiguous B, no copy
+        if b is not None:
+            y += b
     calls["chunked"] += 1
     return y.view(*x.shape[:-1], w.shape[0])
 

@@ -70,7 +70,7 @@ def main(argv=None) -> int:
               ("handoff_per_thread_arrive", 27, 2), ("mma_issue_commit_only", 28, 2),
               ("chunk_pipeline_pairs", 40, 2), ("chunk_pipeline_turn_groups_16warp", 41, 4),
               ("chunk_pipeline_pairs_16warp", 42, 4), ("chunk_pipeline_pairs_16warp_pipelined", 43, 4),
-              ("chunk_pipeline_wide_n256_16warp", 45, 4)]
+              ("chunk_pipeline_wide_n256_16warp", 45, 4), ("chunk_pipeline_pairs_split_n_16warp", 46, 4)]
     for name, mode, epi in probes:
         sms, ms, tflops, clk = run(mode, epi, a.chunks, a.reps, dev)
         mhz = clk.get("sm_mhz")

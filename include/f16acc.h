@@ -110,6 +110,22 @@ int f16acc_gemm_redo(const void *A, int64_t sAm, int64_t sAk,
                      void *workspace, size_t ws_bytes, int device, void *stream,
                      int variant);
 
+/* C[M,N] = A[M,K] @ B[K,N] + bias[N] with the bias added in the epilogue of
+ * both passes.  Replaces patch.py:28-30 (`y = mm(x2, w.t()); y += b`, a
+ * second full read and write of y): the product is rounded to c_dtype, the
+ * FP16 bias (element stride sbias) added in FP32 and the sum rounded again,
+ * so C is bit-identical to the unfused mm + in-place add.  Flags and the redo
+ * pass see the product only (the bias cannot raise a flag, as in the
+ * reference).  bias must be non-NULL unless M or N is 0; other arguments as
+ * f16acc_gemm_ex. */
+int f16acc_gemm_bias(const void *A, int64_t sAm, int64_t sAk,
+                     const void *B, int64_t sBk, int64_t sBn,
+                     const void *bias, int64_t sbias,
+                     void *C, int64_t sCm, int64_t sCn, int c_dtype,
+                     int64_t M, int64_t N, int64_t K, int chunked,
+                     void *workspace, size_t ws_bytes, int device, void *stream,
+                     int variant);
+
 /* Fused GEMM + all-gather for an N-column-sharded product (no reference
  * counterpart; the reference is single-GPU).  This rank computes
  * A[M,K] @ B_shard[K,N] and stores every finished tile into n_outs output
@@ -173,7 +189,9 @@ int f16acc_set_sm_limit(int max_sms);
  * two chunks); 41 = chunk pipeline with 16 epilogue warps, two per (lane
  * quarter, column slice) taking alternate chunks (epi_split 4); 42 / 43 =
  * pairs with 16 epilogue warps, plain / software pipelined (epi_split 4);
- * 45 = 128x256 chunks (N=256 MMAs, 2 TMEM buffers), 16 epilogue warps.
+ * 45 = 128x256 chunks (N=256 MMAs, 2 TMEM buffers), 16 epilogue warps;
+ * 46 = pairs handed over per N-half (N=64 MMAs, one commit per half),
+ * 16 epilogue warps.
  * Warp-level mma.sync rate (grid blocks of 8
  * warps, 8 m16n8k16 chains per warp, `chunks` iterations): 30 = FP16
  * accumulate, 31 = FP32 accumulate, 32 = FP16 chunks of 2 steps added into FP32;
