@@ -127,6 +127,10 @@ int usable_sms(int sms) {
     return lim > 0 && lim < sms ? lim : sms;
 }
 TcShape tc_shape() { return TcShape{g_tc_bn.load(std::memory_order_relaxed), g_tc_epi.load(std::memory_order_relaxed)}; }
+
+// Where flagged tiles of a chunked tcgen05 call are redone: 1 = inside the main
+// kernel, each CTA after its own main tiles; 0 = a second, dependent launch.
+std::atomic<int> g_redo_mode{F16ACC_REDO_INLINE};
 constexpr int kGroupM = 8;
 
 int choose_variant(const Layout& L, int64_t M, int64_t N, int64_t K, int requested) {
@@ -236,10 +240,14 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
         const int64_t tiles = int64_t(p.tiles_m) * p.tiles_n;
         const int sms = usable_sms(info->sms);
         const int grid = int(tiles < sms ? tiles : sms);
+        // Both passes in one launch when the caller wants both and every CTA's
+        // tiles fit the kernel's redo bitmask.
+        p.inline_redo = chunked && phases == kPhaseBoth && cdiv(tiles, grid) <= kMaxLocalTiles &&
+                        g_redo_mode.load(std::memory_order_relaxed) == F16ACC_REDO_INLINE;
         if ((phases & kPhaseMain) &&
             launch_tc(p, shape, chunked != 0, b_mn, c_dtype, false, grid, stream) != cudaSuccess)
             return F16ACC_ERR_CUDA;
-        if (chunked && (phases & kPhaseRedo) &&
+        if (chunked && (phases & kPhaseRedo) && !p.inline_redo &&
             launch_tc(p, shape, false, b_mn, c_dtype, true, grid, stream) != cudaSuccess)
             return F16ACC_ERR_CUDA;
         return F16ACC_OK;
@@ -394,6 +402,11 @@ int f16acc_set_sm_limit(int max_sms) {
     if (max_sms < 0) return F16ACC_ERR_INVALID_ARGUMENT;
     const int prev = g_sm_limit.exchange(max_sms);
     return prev;
+}
+
+int f16acc_set_redo_mode(int mode) {
+    if (mode != F16ACC_REDO_SEPARATE && mode != F16ACC_REDO_INLINE) return F16ACC_ERR_INVALID_ARGUMENT;
+    return g_redo_mode.exchange(mode);
 }
 
 int f16acc_set_tc_config(int tile_n, int epi_split) {

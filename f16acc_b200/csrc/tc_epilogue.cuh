@@ -119,6 +119,31 @@ __device__ __forceinline__ bool consume_chunk_pairs(float (&acc)[CW], int nchunk
     return true;
 }
 
+// One FP32 accumulator (a whole redo tile) handed over through the pair ring:
+// it sits in the pair's first chunk buffer.  Returns false when the wait gave up.
+template <int CW>
+__device__ __forceinline__ bool consume_fp32_pair(float (&acc)[CW], PairRing<CW>& ring, int lane,
+                                                  volatile int* abort, int* status) {
+    const bool ok = mbar_wait(&ring.tfull[ring.p], ring.phase, abort, status, kStatusTimeoutEpilogue);
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    tc_fence_after();
+    const uint32_t a0 = ring.col_base + (2 * ring.p) * ring.stride;
+#pragma unroll
+    for (int j = 0; j < CW / 32; ++j) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(a0 + j * 32, r);
+        tmem_wait_ld();
+        reg_fence(r);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) acc[j * 32 + k] = __uint_as_float(r[k]);
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ring.tempty[ring.p]);
+    ring.advance();
+    return true;
+}
+
 // Sum `nchunks` chunk accumulators into acc (FP32), consuming them from the
 // ring in order.  Returns false when a wait gave up (nothing in flight then).
 template <int CW, typename Ring>

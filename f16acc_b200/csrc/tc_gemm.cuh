@@ -55,7 +55,14 @@ struct TcParams {
     // added to the FP32 result before the cast (nn.Linear's y = x W^T + b).
     const __half* bias;
     int64_t sbias;
+    // Chunked mode: after its main tiles each CTA recomputes its own flagged
+    // tiles in FP32 mode in the same launch (no second kernel, no wait for the
+    // whole grid).  Needs ceil(tiles / grid) <= kMaxLocalTiles.
+    int inline_redo;
 };
+
+// Tiles one CTA can track for the in-kernel redo (a bitmask in smem).
+constexpr int kMaxLocalTiles = 1024;
 
 template <int BN_, int EPI_SPLIT_, int OUT_>
 struct TcConfig {
@@ -79,14 +86,14 @@ struct TcConfig {
     static constexpr int TMEM_COLS = 512;
     static constexpr int ACC_COLS = BN;  // one 32-bit TMEM column per accumulator element, f16 or f32
     static constexpr int NBUF = TMEM_COLS / ACC_COLS;
-    static constexpr int BAR_BYTES = 256;
+    static constexpr int BAR_BYTES = 512;  // mbarriers, TMEM slot, abort flag, redo bitmask
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*alignment slack*/ + BAR_BYTES;
     static constexpr int FLAG_BYTES_PER_WARP = kFlagBytesPerTile / EPI_WARPS;  // every slot byte gets written
     static_assert(FLAG_BYTES_PER_WARP * EPI_WARPS == kFlagBytesPerTile &&
                       (FLAG_BYTES_PER_WARP == 1 || FLAG_BYTES_PER_WARP == 2),
                   "flag slot split over the epilogue warps");
     static_assert(CW == 32 || CW % 64 == 0, "epilogue column slice");
-    static_assert((2 * STAGES + 2 * NBUF + 2) * 8 + 16 <= BAR_BYTES, "barrier area");
+    static_assert((2 * STAGES + 2 * NBUF + 3) * 8 + 8 + kMaxLocalTiles / 8 <= BAR_BYTES, "barrier area");
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 };
 
@@ -166,8 +173,10 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
     uint64_t* tempty = tfull + NBUF;
     uint64_t* drain = tempty + NBUF;
     uint64_t* epi_bar = drain + 1;  // epilogue warps meet here around the staged store
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + 1);
+    uint64_t* redo_go = epi_bar + 1;  // in-kernel redo: every main tile's flag is known
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(redo_go + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    uint32_t* redo_mask = tmem_slot + 2;  // bit i: this CTA's i-th tile was flagged
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -183,7 +192,9 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
         }
         mbar_init(drain, 1);
         mbar_init(epi_bar, Cfg::EPI_WARPS);
+        mbar_init(redo_go, Cfg::EPI_WARPS);
         *abort_flag = 0;
+        for (int w = 0; w < kMaxLocalTiles / 32; ++w) redo_mask[w] = 0u;
         fence_mbarrier_init();
         tma_prefetch_desc(&p.tmA);
         tma_prefetch_desc(&p.tmB);
@@ -213,12 +224,9 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
         if (lane == 0) {
             uint32_t s = 0, ph = 0;
             uint32_t pending = 0, pend_parity = 0;  // stages with a load issued, and that load's phase parity
-            for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-                int tm, tn;
-                raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
-                if (REDO && !tile_flagged(p.flags, static_cast<int64_t>(tm) * p.tiles_n + tn)) continue;
+            auto load_tile = [&](int tm, int tn) -> bool {
                 for (int kb = 0; kb < nkb; ++kb) {
-                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.status, kStatusTimeoutProducer)) goto producer_done;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.status, kStatusTimeoutProducer)) return false;
                     mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
                     pending |= 1u << s;
                     pend_parity = (pend_parity & ~(1u << s)) | (ph << s);
@@ -232,6 +240,24 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
                                         kb * BK);
                     }
                     if (++s == STAGES) { s = 0; ph ^= 1u; }
+                }
+                return true;
+            };
+            for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+                int tm, tn;
+                raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+                if (REDO && !tile_flagged(p.flags, static_cast<int64_t>(tm) * p.tiles_n + tn)) continue;
+                if (!load_tile(tm, tn)) goto producer_done;
+            }
+            if constexpr (CHUNKED) {
+                if (p.inline_redo) {  // the flagged tiles again, for the FP32 pass
+                    if (!mbar_wait(redo_go, 0, abort_flag, p.status, kStatusTimeoutProducer)) goto producer_done;
+                    for (int t = blockIdx.x, i = 0; t < tiles; t += gridDim.x, ++i) {
+                        if (!((redo_mask[i >> 5] >> (i & 31)) & 1u)) continue;
+                        int tm, tn;
+                        raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+                        if (!load_tile(tm, tn)) goto producer_done;
+                    }
                 }
             }
         producer_done:
@@ -301,6 +327,40 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
                     if (++b == NBUF) { b = 0; tph ^= 1u; }
                 }
             }
+            if constexpr (CHUNKED) {
+                if (p.inline_redo) {
+                    // Flagged tiles in FP32 mode: the same K16 MMA sequence as the FP32
+                    // kernel (so bit-identical results), accumulated in chunk buffer 2b
+                    // and handed over through pair b like one chunk pair.
+                    constexpr uint32_t idesc32 = idesc_f16(true, B_MN, BM, BN);
+                    if (!mbar_wait(redo_go, 0, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
+                    for (int t = blockIdx.x, i = 0; t < tiles; t += gridDim.x, ++i) {
+                        if (!((redo_mask[i >> 5] >> (i & 31)) & 1u)) continue;
+                        if (!mbar_wait(&tempty[b], tph ^ 1u, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
+                        tc_fence_after();
+                        const uint32_t d = tmem + (2 * b) * Cfg::ACC_COLS;
+                        for (int kb = 0; kb < nkb; ++kb) {
+                            if (!mbar_wait(&full[s], ph, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
+                            tc_fence_after();
+#pragma unroll
+                            for (int ks = 0; ks < BK / 16; ++ks) {
+                                const int k16 = kb * (BK / 16) + ks;
+                                if (k16 >= nk16) break;
+                                const uint64_t ad = sdesc_sw128(sA0 + s * Cfg::A_BYTES + ks * 32, 16, 1024);
+                                const uint64_t bd = B_MN
+                                                        ? sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 2048, 64 * BK * 2, 1024)
+                                                        : sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 32, 16, 1024);
+                                umma_f16(d, ad, bd, idesc32, k16 > 0 ? 1u : 0u);
+                            }
+                            umma_commit(&empty[s]);
+                            if (++s == STAGES) { s = 0; ph ^= 1u; }
+                        }
+                        umma_commit(&tfull[b]);
+                        b ^= 1u;
+                        if (b == 0) tph ^= 1u;
+                    }
+                }
+            }
         mma_done:
             // All MMAs issued by this thread complete before TMEM is freed.
             umma_commit(drain);
@@ -317,51 +377,19 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
         uint32_t epi_phase = 0;
         ChunkRing<NBUF> ring{tfull, tempty, tmem + lane_base + colg * CW, Cfg::ACC_COLS};    // FP32 mode
         PairRing<CW> pairs{tfull, tempty, tmem + lane_base + colg * CW, Cfg::ACC_COLS};     // chunked mode
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-            int tm, tn;
-            raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
-            const int64_t tile_id = static_cast<int64_t>(tm) * p.tiles_n + tn;
-            if (REDO && !tile_flagged(p.flags, tile_id)) continue;
-            float acc[CW];
-            if constexpr (CHUNKED) {
-#pragma unroll
-                for (int j = 0; j < CW; ++j) acc[j] = 0.0f;
-                if (!consume_chunk_pairs<CW>(acc, nchunks, pairs, lane, abort_flag, p.status)) break;
-                float z = 0.0f;
-#pragma unroll
-                for (int j = 0; j < CW; ++j) z = nonfinite_probe(z, acc[j]);
-                const bool bad = __any_sync(0xffffffffu, z != z);
-                if (lane == 0) {
-                    uint8_t* slot = p.flags + tile_id * kFlagBytesPerTile;
-                    if constexpr (Cfg::FLAG_BYTES_PER_WARP == 2)
-                        *reinterpret_cast<uint16_t*>(slot + 2 * e) = bad ? 1 : 0;
-                    else
-                        slot[e] = bad ? 1 : 0;
-                }
-            } else {
-                if (!ring.wait_full(abort_flag, p.status)) break;
-#pragma unroll
-                for (int j = 0; j < CW / 32; ++j) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(ring.addr() + j * 32, r);
-                    tmem_wait_ld();
-                    reg_fence(r);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) acc[j * 32 + i] = __uint_as_float(r[i]);
-                }
-                ring.release(lane);
-            }
-            // Stage the tile in smem (rounded to the output type), then copy it out to C
-            // and to every peer's buffer (fused all-gather): whole rows in coalesced
-            // 16-byte-per-lane stores when C allows, else element by element.  The bias
-            // (after the flag: the reference adds it outside the kernel) goes on in the
-            // copy-out, to the product already rounded to the output type.
+        // Stage the tile in smem (rounded to the output type), then copy it out to C
+        // and to every peer's buffer (fused all-gather): whole rows in coalesced
+        // 16-byte-per-lane stores when C allows, else element by element.  The bias
+        // (after the flag: the reference adds it outside the kernel) goes on in the
+        // copy-out, to the product already rounded to the output type.  False when
+        // a wait gave up.
+        auto emit = [&](const float (&acc)[CW], int tm, int tn) -> bool {
             stage_row<OUT, CW, Cfg::STAGE_PITCH>(staging, q * 32 + lane, colg * CW, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(epi_bar);
             if (!__all_sync(0xffffffffu,
                             mbar_wait(epi_bar, epi_phase, abort_flag, p.status, kStatusTimeoutEpilogue)))
-                break;
+                return false;
             epi_phase ^= 1u;
             if (p.c_vec)
                 store_staged<OUT, BM, BN, Cfg::STAGE_PITCH, Cfg::EPI_WARPS>(
@@ -374,8 +402,74 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
             if (lane == 0) mbar_arrive(epi_bar);  // staging free again once every warp has copied out
             if (!__all_sync(0xffffffffu,
                             mbar_wait(epi_bar, epi_phase, abort_flag, p.status, kStatusTimeoutEpilogue)))
-                break;
+                return false;
             epi_phase ^= 1u;
+            return true;
+        };
+        bool alive = true;
+        for (int t = blockIdx.x, i = 0; t < tiles; t += gridDim.x, ++i) {
+            int tm, tn;
+            raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+            const int64_t tile_id = static_cast<int64_t>(tm) * p.tiles_n + tn;
+            if (REDO && !tile_flagged(p.flags, tile_id)) continue;
+            float acc[CW];
+            if constexpr (CHUNKED) {
+#pragma unroll
+                for (int j = 0; j < CW; ++j) acc[j] = 0.0f;
+                if (!consume_chunk_pairs<CW>(acc, nchunks, pairs, lane, abort_flag, p.status)) {
+                    alive = false;
+                    break;
+                }
+                float z = 0.0f;
+#pragma unroll
+                for (int j = 0; j < CW; ++j) z = nonfinite_probe(z, acc[j]);
+                const bool bad = __any_sync(0xffffffffu, z != z);
+                if (lane == 0) {
+                    uint8_t* slot = p.flags + tile_id * kFlagBytesPerTile;
+                    if constexpr (Cfg::FLAG_BYTES_PER_WARP == 2)
+                        *reinterpret_cast<uint16_t*>(slot + 2 * e) = bad ? 1 : 0;
+                    else
+                        slot[e] = bad ? 1 : 0;
+                    if (bad && p.inline_redo) atomicOr(&redo_mask[i >> 5], 1u << (i & 31));
+                }
+            } else {
+                if (!ring.wait_full(abort_flag, p.status)) {
+                    alive = false;
+                    break;
+                }
+#pragma unroll
+                for (int j = 0; j < CW / 32; ++j) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(ring.addr() + j * 32, r);
+                    tmem_wait_ld();
+                    reg_fence(r);
+#pragma unroll
+                    for (int k = 0; k < 32; ++k) acc[j * 32 + k] = __uint_as_float(r[k]);
+                }
+                ring.release(lane);
+            }
+            if (!emit(acc, tm, tn)) {
+                alive = false;
+                break;
+            }
+        }
+        if constexpr (CHUNKED) {
+            if (alive && p.inline_redo) {
+                // Every warp has set its mask bits for every main tile; the producer and
+                // MMA warps wait on the same barrier, so all roles redo the same tiles.
+                __syncwarp();
+                if (lane == 0) mbar_arrive(redo_go);
+                if (__all_sync(0xffffffffu, mbar_wait(redo_go, 0, abort_flag, p.status, kStatusTimeoutEpilogue))) {
+                    for (int t = blockIdx.x, i = 0; t < tiles; t += gridDim.x, ++i) {
+                        if (!((redo_mask[i >> 5] >> (i & 31)) & 1u)) continue;
+                        int tm, tn;
+                        raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+                        float acc[CW];
+                        if (!consume_fp32_pair<CW>(acc, pairs, lane, abort_flag, p.status)) break;
+                        if (!emit(acc, tm, tn)) break;
+                    }
+                }
+            }
         }
         // peer stores become visible system-wide before the kernel is seen complete
         if (p.n_peers > 0) __threadfence_system();

@@ -169,6 +169,18 @@ int f16acc_set_tc_config(int tile_n, int epi_split);
  * that overlaps a sharded product.  Returns the previous cap. */
 int f16acc_set_sm_limit(int max_sms);
 
+/* Where a chunked tcgen05 call (f16acc_gemm, _ex, _bias, _allgather,
+ * _noalloc) redoes its flagged tiles, process-wide, for later calls:
+ * F16ACC_REDO_INLINE (the default) = inside the main kernel, each CTA
+ * recomputing its own flagged tiles in FP32 mode after its main tiles, one
+ * launch in all; F16ACC_REDO_SEPARATE = the reference's shape, a second
+ * launch over the flags (kernel.py:100-104).  Results are bit-identical either
+ * way.  f16acc_gemm_main / _redo always make the two separate launches.
+ * Returns the previous mode. */
+#define F16ACC_REDO_SEPARATE 0
+#define F16ACC_REDO_INLINE 1
+int f16acc_set_redo_mode(int mode);
+
 /* Raw-rate probe, the B200 counterpart of the reference's bench/rate.py and
  * bench/chunkrate.py: `grid` CTAs (one per SM) each run `chunks` 32-long
  * chunks of 128x128 tcgen05 MMAs on a fixed shared-memory tile.  mode 0: MMA
