@@ -42,6 +42,7 @@ SIGNATURES = {
     "f16acc_set_tc_config": (_int, [_int, _int]),
     "f16acc_set_sm_limit": (_int, [_int]),
     "f16acc_set_redo_mode": (_int, [_int]),
+    "f16acc_set_schedule": (_int, [_int]),
     "f16acc_probe_chunk_rate": (_int, [_int, _int, _int, _int, _p, _int, _p]),
     "f16acc_device_status": (_int, [_int, _int]),
     "f16acc_gemm_noalloc": (_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _int, _i64, _i64, _i64, _int,
@@ -61,6 +62,7 @@ NOALLOC_MAX_TILES = 65536
 OUT_F16, OUT_F32, OUT_BF16 = 0, 1, 2
 VARIANT_AUTO, VARIANT_TCGEN05, VARIANT_MMA_SYNC = 0, 1, 2
 REDO_SEPARATE, REDO_INLINE = 0, 1
+SCHEDULE_STATIC, SCHEDULE_DYNAMIC = 0, 1
 
 _lib = None
 _lock = threading.Lock()

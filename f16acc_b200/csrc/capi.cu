@@ -131,6 +131,9 @@ TcShape tc_shape() { return TcShape{g_tc_bn.load(std::memory_order_relaxed), g_t
 // Where flagged tiles of a chunked tcgen05 call are redone: 1 = inside the main
 // kernel, each CTA after its own main tiles; 0 = a second, dependent launch.
 std::atomic<int> g_redo_mode{F16ACC_REDO_INLINE};
+
+// Tile order of the chunked main pass (F16ACC_SCHEDULE_*).
+std::atomic<int> g_schedule{F16ACC_SCHEDULE_DYNAMIC};
 constexpr int kGroupM = 8;
 
 int choose_variant(const Layout& L, int64_t M, int64_t N, int64_t K, int requested) {
@@ -238,15 +241,22 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
         p.bias = static_cast<const __half*>(bias);
         p.sbias = sbias;
         const int64_t tiles = int64_t(p.tiles_m) * p.tiles_n;
+        if (tiles >= (int64_t(1) << 31)) return F16ACC_ERR_INVALID_ARGUMENT;
         const int sms = usable_sms(info->sms);
         const int grid = int(tiles < sms ? tiles : sms);
-        // Both passes in one launch when the caller wants both and every CTA's
-        // tiles fit the kernel's redo bitmask.
-        p.inline_redo = chunked && phases == kPhaseBoth && cdiv(tiles, grid) <= kMaxLocalTiles &&
+        // Both passes in one launch when the caller wants both.
+        p.inline_redo = chunked && phases == kPhaseBoth &&
                         g_redo_mode.load(std::memory_order_relaxed) == F16ACC_REDO_INLINE;
+        // The chunked main pass takes its tiles dynamically (one CTA launched per
+        // tile, running CTAs take over the tiles of CTAs not started yet) unless
+        // an SM cap asks for a bounded persistent grid.
+        p.dyn_sched = chunked && tiles > grid && g_sm_limit.load(std::memory_order_relaxed) == 0 &&
+                      g_schedule.load(std::memory_order_relaxed) == F16ACC_SCHEDULE_DYNAMIC;
         if ((phases & kPhaseMain) &&
-            launch_tc(p, shape, chunked != 0, b_mn, c_dtype, false, grid, stream) != cudaSuccess)
+            launch_tc(p, shape, chunked != 0, b_mn, c_dtype, false, p.dyn_sched ? int(tiles) : grid, stream) !=
+                cudaSuccess)
             return F16ACC_ERR_CUDA;
+        p.dyn_sched = 0;  // the separate redo pass walks the flags in static order
         if (chunked && (phases & kPhaseRedo) && !p.inline_redo &&
             launch_tc(p, shape, false, b_mn, c_dtype, true, grid, stream) != cudaSuccess)
             return F16ACC_ERR_CUDA;
@@ -407,6 +417,11 @@ int f16acc_set_sm_limit(int max_sms) {
 int f16acc_set_redo_mode(int mode) {
     if (mode != F16ACC_REDO_SEPARATE && mode != F16ACC_REDO_INLINE) return F16ACC_ERR_INVALID_ARGUMENT;
     return g_redo_mode.exchange(mode);
+}
+
+int f16acc_set_schedule(int mode) {
+    if (mode != F16ACC_SCHEDULE_STATIC && mode != F16ACC_SCHEDULE_DYNAMIC) return F16ACC_ERR_INVALID_ARGUMENT;
+    return g_schedule.exchange(mode);
 }
 
 int f16acc_set_tc_config(int tile_n, int epi_split) {

@@ -19,6 +19,8 @@ enum DeviceStatus : int {
     kStatusTimeoutMma = 0x102,        // MMA warp waited too long for data or a free TMEM buffer
     kStatusTimeoutEpilogue = 0x103,   // epilogue waited too long for an accumulator
     kStatusTimeoutProbe = 0x104,      // a probe kernel's wait ran out
+    kStatusTimeoutSchedule = 0x105,   // the tile scheduler waited too long for the epilogue's flag decisions
+    kStatusRedoQueueFull = 0x106,     // in-kernel redo queue overflow (a bug; the kernel stops)
 };
 
 // A wait gives up after this many nanoseconds of %globaltimer.  The longest
@@ -239,6 +241,36 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool d_f32, bool b_mn_major, in
 // ---------------------------------------------------------------- grid dependency control (PDL)
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------- dynamic tile scheduling
+// Cluster launch control (sm_100): ask the hardware to cancel one CTA of this
+// grid that has not started yet; the 16-byte response lands in `resp16` (smem,
+// 16-byte aligned) and completes 16 bytes of transaction on `bar`, which the
+// caller armed with mbar_arrive_expect_tx(bar, 16).  Never issued again after
+// a response that reports failure.
+__device__ __forceinline__ void clc_try_cancel(void* resp16, uint64_t* bar) {
+    asm volatile("clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];" ::"r"(
+                     smem_u32(resp16)),
+                 "r"(smem_u32(bar))
+                 : "memory");
+}
+// Decode a landed response: true and the cancelled CTA's blockIdx.x (whose work
+// the caller now owns), or false when no CTA was left to cancel.
+__device__ __forceinline__ bool clc_query(const void* resp16, uint32_t& ctaid_x) {
+    uint32_t ok, x = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b128 r;\n\t"
+        "ld.shared.b128 r, [%2];\n\t"
+        "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t"
+        "@p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, r;\n\t"
+        "}"
+        : "=r"(ok), "+r"(x)
+        : "r"(smem_u32(resp16))
+        : "memory");
+    ctaid_x = x;
+    return ok != 0;
+}
 
 // ---------------------------------------------------------------- arithmetic
 // acc += (float)h for the two FP16 halves of `packed` (low half -> a0).  One

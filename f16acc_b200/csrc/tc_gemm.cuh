@@ -55,14 +55,39 @@ struct TcParams {
     // added to the FP32 result before the cast (nn.Linear's y = x W^T + b).
     const __half* bias;
     int64_t sbias;
-    // Chunked mode: after its main tiles each CTA recomputes its own flagged
-    // tiles in FP32 mode in the same launch (no second kernel, no wait for the
-    // whole grid).  Needs ceil(tiles / grid) <= kMaxLocalTiles.
+    // Chunked mode: a CTA recomputes the tiles it flagged in FP32 mode within
+    // the same launch, between its main tiles (no second kernel, no wait for
+    // the whole grid).
     int inline_redo;
+    // Tile order.  0: static, the grid is persistent and CTA i takes tiles
+    // i, i + grid, ...  1: dynamic, one CTA per tile is launched and a running
+    // CTA takes over the tile of a CTA not yet started (cluster launch
+    // control), so a CTA slowed by redo work takes fewer main tiles.
+    int dyn_sched;
 };
 
-// Tiles one CTA can track for the in-kernel redo (a bitmask in smem).
-constexpr int kMaxLocalTiles = 1024;
+// Work items the producer warp hands to the MMA warp and the epilogue.
+enum TcWork : int { kWorkMain = 0, kWorkRedo = 1, kWorkEnd = 2 };
+constexpr int kSchedDepth = 4;   // work items in flight between the roles
+constexpr int kRedoQueue = 32;   // flagged tiles waiting for their FP32 redo (bounded by the pipeline depth)
+
+// Control block at the end of the kernel's shared memory.
+template <int STAGES, int NBUF>
+struct alignas(16) TcCtrl {
+    uint4 clc_resp;                    // cluster launch control response
+    int4 sched[kSchedDepth];           // {tm, tn, kind, 0}
+    int2 redo_q[kRedoQueue];           // {tm, tn} of flagged tiles
+    uint64_t full[STAGES], empty[STAGES];
+    uint64_t tfull[NBUF], tempty[NBUF];
+    uint64_t sched_full[kSchedDepth], sched_empty[kSchedDepth];
+    uint64_t clc_bar, drain, epi_bar;
+    uint32_t tmem_slot;
+    int abort_flag;
+    int rq_tail;                       // redo items pushed (epilogue)
+    int rq_head;                       // redo items taken (producer)
+    int main_done;                     // main tiles whose flag is decided (epilogue)
+    int tile_bad[2];                   // per-tile OR of the warps' flags, double-buffered
+};
 
 template <int BN_, int EPI_SPLIT_, int OUT_>
 struct TcConfig {
@@ -86,14 +111,13 @@ struct TcConfig {
     static constexpr int TMEM_COLS = 512;
     static constexpr int ACC_COLS = BN;  // one 32-bit TMEM column per accumulator element, f16 or f32
     static constexpr int NBUF = TMEM_COLS / ACC_COLS;
-    static constexpr int BAR_BYTES = 512;  // mbarriers, TMEM slot, abort flag, redo bitmask
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*alignment slack*/ + BAR_BYTES;
+    using Ctrl = TcCtrl<STAGES, NBUF>;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*alignment slack*/ + int(sizeof(Ctrl));
     static constexpr int FLAG_BYTES_PER_WARP = kFlagBytesPerTile / EPI_WARPS;  // every slot byte gets written
     static_assert(FLAG_BYTES_PER_WARP * EPI_WARPS == kFlagBytesPerTile &&
                       (FLAG_BYTES_PER_WARP == 1 || FLAG_BYTES_PER_WARP == 2),
                   "flag slot split over the epilogue warps");
     static_assert(CW == 32 || CW % 64 == 0, "epilogue column slice");
-    static_assert((2 * STAGES + 2 * NBUF + 3) * 8 + 8 + kMaxLocalTiles / 8 <= BAR_BYTES, "barrier area");
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 };
 
@@ -167,16 +191,17 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
     uint8_t* staging = smem + STAGES * Cfg::STAGE_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(staging + Cfg::STAGING_BYTES);
-    uint64_t* empty = full + STAGES;
-    uint64_t* tfull = empty + STAGES;
-    uint64_t* tempty = tfull + NBUF;
-    uint64_t* drain = tempty + NBUF;
-    uint64_t* epi_bar = drain + 1;  // epilogue warps meet here around the staged store
-    uint64_t* redo_go = epi_bar + 1;  // in-kernel redo: every main tile's flag is known
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(redo_go + 1);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    uint32_t* redo_mask = tmem_slot + 2;  // bit i: this CTA's i-th tile was flagged
+    auto* ctrl = reinterpret_cast<typename Cfg::Ctrl*>(staging + Cfg::STAGING_BYTES);
+    uint64_t* full = ctrl->full;
+    uint64_t* empty = ctrl->empty;
+    uint64_t* tfull = ctrl->tfull;
+    uint64_t* tempty = ctrl->tempty;
+    uint64_t* drain = &ctrl->drain;
+    uint64_t* epi_bar = &ctrl->epi_bar;  // epilogue warps meet here around the staged store
+    volatile int* abort_flag = &ctrl->abort_flag;
+    volatile int* rq_tail = &ctrl->rq_tail;
+    volatile int* rq_head = &ctrl->rq_head;
+    volatile int* main_done = &ctrl->main_done;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -190,23 +215,30 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], Cfg::EPI_WARPS);
         }
+        for (int i = 0; i < kSchedDepth; ++i) {
+            mbar_init(&ctrl->sched_full[i], 1);
+            mbar_init(&ctrl->sched_empty[i], 1 + Cfg::EPI_WARPS);  // the MMA thread and every epilogue warp
+        }
+        mbar_init(&ctrl->clc_bar, 1);
         mbar_init(drain, 1);
         mbar_init(epi_bar, Cfg::EPI_WARPS);
-        mbar_init(redo_go, Cfg::EPI_WARPS);
         *abort_flag = 0;
-        for (int w = 0; w < kMaxLocalTiles / 32; ++w) redo_mask[w] = 0u;
+        *rq_tail = 0;
+        *rq_head = 0;
+        *main_done = 0;
+        ctrl->tile_bad[0] = ctrl->tile_bad[1] = 0;
         fence_mbarrier_init();
         tma_prefetch_desc(&p.tmA);
         tma_prefetch_desc(&p.tmB);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+        tmem_alloc(&ctrl->tmem_slot, Cfg::TMEM_COLS);
         tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
+    const uint32_t tmem = ctrl->tmem_slot;
 
     if constexpr (REDO) {
         grid_dep_wait();  // flags and C come from the main pass
@@ -243,40 +275,147 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
                 }
                 return true;
             };
-            for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-                int tm, tn;
-                raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
-                if (REDO && !tile_flagged(p.flags, static_cast<int64_t>(tm) * p.tiles_n + tn)) continue;
-                if (!load_tile(tm, tn)) goto producer_done;
-            }
-            if constexpr (CHUNKED) {
-                if (p.inline_redo) {  // the flagged tiles again, for the FP32 pass
-                    if (!mbar_wait(redo_go, 0, abort_flag, p.status, kStatusTimeoutProducer)) goto producer_done;
-                    for (int t = blockIdx.x, i = 0; t < tiles; t += gridDim.x, ++i) {
-                        if (!((redo_mask[i >> 5] >> (i & 31)) & 1u)) continue;
-                        int tm, tn;
+            // ---- tile scheduler: this thread decides the CTA's work items, in order,
+            // and publishes each to the MMA warp and the epilogue through ctrl->sched.
+            const bool inline_redo = CHUNKED && p.inline_redo != 0;
+            int next_static = blockIdx.x;  // static order: this CTA's next main tile
+            bool clc_inflight = false;     // a cancel request not yet answered
+            uint32_t clc_phase = 0;
+            int issued_main = 0, taken = 0;
+            auto clc_ask = [&]() {
+                mbar_arrive_expect_tx(&ctrl->clc_bar, 16);
+                clc_try_cancel(&ctrl->clc_resp, &ctrl->clc_bar);
+                clc_inflight = true;
+            };
+            auto pop_redo = [&](int& tm, int& tn) -> bool {
+                if (taken == *rq_tail) return false;
+                __threadfence_block();  // the entry was written before the tail moved
+                const int2 w = ctrl->redo_q[taken % kRedoQueue];
+                tm = w.x;
+                tn = w.y;
+                *rq_head = ++taken;
+                return true;
+            };
+            // Every main tile issued here has had its flag decided by the epilogue.
+            auto wait_flags_decided = [&]() -> bool {
+                const uint64_t t0 = globaltimer_ns();
+                while (*main_done != issued_main) {
+                    if (*abort_flag) return false;
+                    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                        atomicCAS(p.status, 0, kStatusTimeoutSchedule);
+                        *abort_flag = 1;
+                        return false;
+                    }
+                    __nanosleep(128);
+                }
+                return true;
+            };
+            // The next work item: a finished flagged tile's redo first, then a new
+            // main tile, then (main tiles exhausted) the redo items still to come,
+            // then the end.  False when a wait gave up.
+            auto next_work = [&](int& kind, int& tm, int& tn) -> bool {
+                kind = kWorkRedo;
+                if (inline_redo && pop_redo(tm, tn)) return true;
+                kind = kWorkMain;
+                if (p.dyn_sched) {
+                    if (clc_inflight) {
+                        if (!mbar_wait(&ctrl->clc_bar, clc_phase, abort_flag, p.status, kStatusTimeoutProducer))
+                            return false;
+                        clc_phase ^= 1u;
+                        clc_inflight = false;
+                        uint32_t cta;
+                        if (clc_query(&ctrl->clc_resp, cta)) {  // that CTA's tile is ours now
+                            clc_ask();
+                            raster(static_cast<int>(cta), p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+                            return true;
+                        }
+                    }
+                } else {
+                    while (next_static < tiles) {
+                        const int t = next_static;
+                        next_static += gridDim.x;
                         raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
-                        if (!load_tile(tm, tn)) goto producer_done;
+                        if (REDO && !tile_flagged(p.flags, static_cast<int64_t>(tm) * p.tiles_n + tn)) continue;
+                        return true;
                     }
                 }
+                kind = kWorkRedo;
+                if (inline_redo) {
+                    if (!wait_flags_decided()) return false;
+                    if (pop_redo(tm, tn)) return true;
+                }
+                kind = kWorkEnd;
+                return true;
+            };
+            int kind, tm, tn;
+            if (p.dyn_sched) {  // this CTA's own tile first, the next one asked for meanwhile
+                kind = kWorkMain;
+                raster(blockIdx.x, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+                clc_ask();
+            } else if (!next_work(kind, tm, tn)) {
+                goto producer_done;
+            }
+            for (uint32_t qi = 0, qph = 0;;) {
+                if (!mbar_wait(&ctrl->sched_empty[qi], qph ^ 1u, abort_flag, p.status, kStatusTimeoutProducer))
+                    goto producer_done;
+                ctrl->sched[qi] = make_int4(tm, tn, kind, 0);
+                mbar_arrive(&ctrl->sched_full[qi]);
+                if (++qi == kSchedDepth) { qi = 0; qph ^= 1u; }
+                if (kind == kWorkEnd) break;
+                if (kind == kWorkMain) ++issued_main;
+                if (!load_tile(tm, tn)) goto producer_done;
+                if (!next_work(kind, tm, tn)) goto producer_done;
             }
         producer_done:
             // Let every copy this CTA issued land before the CTA can exit
             // (they already have on a normal exit; this matters after an abort).
             for (int st = 0; st < STAGES; ++st)
                 if (pending & (1u << st)) mbar_wait_drain(&full[st], (pend_parity >> st) & 1u);
+            if (clc_inflight) mbar_wait_drain(&ctrl->clc_bar, clc_phase);  // only after an abort
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16(!CHUNKED, B_MN, BM, BN);
+            constexpr uint32_t idesc32 = idesc_f16(true, B_MN, BM, BN);
             const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
             uint32_t s = 0, ph = 0, b = 0, tph = 0;
-            for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-                int tm, tn;
-                raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
-                if (REDO && !tile_flagged(p.flags, static_cast<int64_t>(tm) * p.tiles_n + tn)) continue;
-                if constexpr (CHUNKED) {
+            // A whole tile's K loop with an FP32 accumulator in TMEM at d.
+            auto fp32_tile = [&](uint32_t d) -> bool {
+                for (int kb = 0; kb < nkb; ++kb) {
+                    if (!mbar_wait(&full[s], ph, abort_flag, p.status, kStatusTimeoutMma)) return false;
+                    tc_fence_after();
+#pragma unroll
+                    for (int ks = 0; ks < BK / 16; ++ks) {
+                        const int k16 = kb * (BK / 16) + ks;
+                        if (k16 >= nk16) break;
+                        const uint64_t ad = sdesc_sw128(sA0 + s * Cfg::A_BYTES + ks * 32, 16, 1024);
+                        const uint64_t bd = B_MN ? sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 2048, 64 * BK * 2, 1024)
+                                                 : sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 32, 16, 1024);
+                        umma_f16(d, ad, bd, idesc32, k16 > 0 ? 1u : 0u);
+                    }
+                    umma_commit(&empty[s]);
+                    if (++s == STAGES) { s = 0; ph ^= 1u; }
+                }
+                return true;
+            };
+            for (uint32_t qi = 0, qph = 0;;) {
+                if (!mbar_wait(&ctrl->sched_full[qi], qph, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
+                const int kind = ctrl->sched[qi].z;
+                mbar_arrive(&ctrl->sched_empty[qi]);
+                if (++qi == kSchedDepth) { qi = 0; qph ^= 1u; }
+                if (kind == kWorkEnd) break;
+                if (CHUNKED && kind == kWorkRedo) {
+                    // A flagged tile in FP32 mode: the K16 MMA sequence of the FP32 kernel
+                    // (so bit-identical results), accumulated in chunk buffer 2b and handed
+                    // over through pair b like one chunk pair.
+                    if (!mbar_wait(&tempty[b], tph ^ 1u, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
+                    tc_fence_after();
+                    if (!fp32_tile(tmem + (2 * b) * Cfg::ACC_COLS)) goto mma_done;
+                    umma_commit(&tfull[b]);
+                    b ^= 1u;
+                    if (b == 0) tph ^= 1u;
+                } else if constexpr (CHUNKED) {
                     // One hand-off per 64-wide stage: its two 32-long chunks go to the
                     // chunk buffers 2b and 2b+1 of pair b (two pairs in flight), one commit.
                     for (int kb = 0; kb < nkb; ++kb) {
@@ -307,58 +446,9 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
                 } else {
                     if (!mbar_wait(&tempty[b], tph ^ 1u, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
                     tc_fence_after();
-                    const uint32_t d = tmem + b * Cfg::ACC_COLS;
-                    for (int kb = 0; kb < nkb; ++kb) {
-                        if (!mbar_wait(&full[s], ph, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
-                        tc_fence_after();
-#pragma unroll
-                        for (int ks = 0; ks < BK / 16; ++ks) {
-                            const int k16 = kb * (BK / 16) + ks;
-                            if (k16 >= nk16) break;
-                            const uint64_t ad = sdesc_sw128(sA0 + s * Cfg::A_BYTES + ks * 32, 16, 1024);
-                            const uint64_t bd = B_MN ? sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 2048, 64 * BK * 2, 1024)
-                                                     : sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 32, 16, 1024);
-                            umma_f16(d, ad, bd, idesc, k16 > 0 ? 1u : 0u);
-                        }
-                        umma_commit(&empty[s]);
-                        if (++s == STAGES) { s = 0; ph ^= 1u; }
-                    }
+                    if (!fp32_tile(tmem + b * Cfg::ACC_COLS)) goto mma_done;
                     umma_commit(&tfull[b]);
                     if (++b == NBUF) { b = 0; tph ^= 1u; }
-                }
-            }
-            if constexpr (CHUNKED) {
-                if (p.inline_redo) {
-                    // Flagged tiles in FP32 mode: the same K16 MMA sequence as the FP32
-                    // kernel (so bit-identical results), accumulated in chunk buffer 2b
-                    // and handed over through pair b like one chunk pair.
-                    constexpr uint32_t idesc32 = idesc_f16(true, B_MN, BM, BN);
-                    if (!mbar_wait(redo_go, 0, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
-                    for (int t = blockIdx.x, i = 0; t < tiles; t += gridDim.x, ++i) {
-                        if (!((redo_mask[i >> 5] >> (i & 31)) & 1u)) continue;
-                        if (!mbar_wait(&tempty[b], tph ^ 1u, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
-                        tc_fence_after();
-                        const uint32_t d = tmem + (2 * b) * Cfg::ACC_COLS;
-                        for (int kb = 0; kb < nkb; ++kb) {
-                            if (!mbar_wait(&full[s], ph, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
-                            tc_fence_after();
-#pragma unroll
-                            for (int ks = 0; ks < BK / 16; ++ks) {
-                                const int k16 = kb * (BK / 16) + ks;
-                                if (k16 >= nk16) break;
-                                const uint64_t ad = sdesc_sw128(sA0 + s * Cfg::A_BYTES + ks * 32, 16, 1024);
-                                const uint64_t bd = B_MN
-                                                        ? sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 2048, 64 * BK * 2, 1024)
-                                                        : sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 32, 16, 1024);
-                                umma_f16(d, ad, bd, idesc32, k16 > 0 ? 1u : 0u);
-                            }
-                            umma_commit(&empty[s]);
-                            if (++s == STAGES) { s = 0; ph ^= 1u; }
-                        }
-                        umma_commit(&tfull[b]);
-                        b ^= 1u;
-                        if (b == 0) tph ^= 1u;
-                    }
                 }
             }
         mma_done:
@@ -383,7 +473,14 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
         // (after the flag: the reference adds it outside the kernel) goes on in the
         // copy-out, to the product already rounded to the output type.  False when
         // a wait gave up.
-        auto emit = [&](const float (&acc)[CW], int tm, int tn) -> bool {
+        //
+        // `decide` (a main tile of the chunked kernel with the in-kernel redo):
+        // once every warp has passed the first barrier its flag is in
+        // tile_bad[par]; epilogue warp 0 queues the tile for its FP32 redo if any
+        // warp saw a non-finite value, then counts the tile as decided.
+        uint32_t par = 0;
+        int decided = 0;
+        auto emit = [&](const float (&acc)[CW], int tm, int tn, bool decide) -> bool {
             stage_row<OUT, CW, Cfg::STAGE_PITCH>(staging, q * 32 + lane, colg * CW, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(epi_bar);
@@ -391,6 +488,24 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
                             mbar_wait(epi_bar, epi_phase, abort_flag, p.status, kStatusTimeoutEpilogue)))
                 return false;
             epi_phase ^= 1u;
+            if (decide) {
+                if (e == 0 && lane == 0) {
+                    if (atomicExch(&ctrl->tile_bad[par], 0) != 0) {
+                        const int tail = *rq_tail;
+                        if (tail - *rq_head >= kRedoQueue) {
+                            atomicCAS(p.status, 0, kStatusRedoQueueFull);
+                            *abort_flag = 1;
+                        } else {
+                            ctrl->redo_q[tail % kRedoQueue] = make_int2(tm, tn);
+                            __threadfence_block();
+                            *rq_tail = tail + 1;
+                        }
+                    }
+                    __threadfence_block();
+                    *main_done = ++decided;
+                }
+                par ^= 1u;
+            }
             if (p.c_vec)
                 store_staged<OUT, BM, BN, Cfg::STAGE_PITCH, Cfg::EPI_WARPS>(
                     staging, dsts, 1 + p.n_peers, p.sCm, tm * BM, tn * BN, p.M, p.N, e, lane, p.bias, p.sbias);
@@ -406,37 +521,41 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
             epi_phase ^= 1u;
             return true;
         };
-        bool alive = true;
-        for (int t = blockIdx.x, i = 0; t < tiles; t += gridDim.x, ++i) {
-            int tm, tn;
-            raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
-            const int64_t tile_id = static_cast<int64_t>(tm) * p.tiles_n + tn;
-            if (REDO && !tile_flagged(p.flags, tile_id)) continue;
+        const bool inline_redo = CHUNKED && p.inline_redo != 0;
+        for (uint32_t qi = 0, qph = 0;;) {
+            if (!__all_sync(0xffffffffu,
+                            mbar_wait(&ctrl->sched_full[qi], qph, abort_flag, p.status, kStatusTimeoutEpilogue)))
+                break;
+            const int4 w = ctrl->sched[qi];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctrl->sched_empty[qi]);
+            if (++qi == kSchedDepth) { qi = 0; qph ^= 1u; }
+            if (w.z == kWorkEnd) break;
+            const int tm = w.x, tn = w.y;
+            const bool main_item = w.z == kWorkMain;
             float acc[CW];
             if constexpr (CHUNKED) {
+                if (main_item) {
 #pragma unroll
-                for (int j = 0; j < CW; ++j) acc[j] = 0.0f;
-                if (!consume_chunk_pairs<CW>(acc, nchunks, pairs, lane, abort_flag, p.status)) {
-                    alive = false;
-                    break;
-                }
-                float z = 0.0f;
+                    for (int j = 0; j < CW; ++j) acc[j] = 0.0f;
+                    if (!consume_chunk_pairs<CW>(acc, nchunks, pairs, lane, abort_flag, p.status)) break;
+                    float z = 0.0f;
 #pragma unroll
-                for (int j = 0; j < CW; ++j) z = nonfinite_probe(z, acc[j]);
-                const bool bad = __any_sync(0xffffffffu, z != z);
-                if (lane == 0) {
-                    uint8_t* slot = p.flags + tile_id * kFlagBytesPerTile;
-                    if constexpr (Cfg::FLAG_BYTES_PER_WARP == 2)
-                        *reinterpret_cast<uint16_t*>(slot + 2 * e) = bad ? 1 : 0;
-                    else
-                        slot[e] = bad ? 1 : 0;
-                    if (bad && p.inline_redo) atomicOr(&redo_mask[i >> 5], 1u << (i & 31));
+                    for (int j = 0; j < CW; ++j) z = nonfinite_probe(z, acc[j]);
+                    const bool bad = __any_sync(0xffffffffu, z != z);
+                    if (lane == 0) {
+                        uint8_t* slot = p.flags + (static_cast<int64_t>(tm) * p.tiles_n + tn) * kFlagBytesPerTile;
+                        if constexpr (Cfg::FLAG_BYTES_PER_WARP == 2)
+                            *reinterpret_cast<uint16_t*>(slot + 2 * e) = bad ? 1 : 0;
+                        else
+                            slot[e] = bad ? 1 : 0;
+                        if (bad && inline_redo) atomicOr(&ctrl->tile_bad[par], 1);
+                    }
+                } else {
+                    if (!consume_fp32_pair<CW>(acc, pairs, lane, abort_flag, p.status)) break;
                 }
             } else {
-                if (!ring.wait_full(abort_flag, p.status)) {
-                    alive = false;
-                    break;
-                }
+                if (!ring.wait_full(abort_flag, p.status)) break;
 #pragma unroll
                 for (int j = 0; j < CW / 32; ++j) {
                     uint32_t r[32];
@@ -448,28 +567,7 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
                 }
                 ring.release(lane);
             }
-            if (!emit(acc, tm, tn)) {
-                alive = false;
-                break;
-            }
-        }
-        if constexpr (CHUNKED) {
-            if (alive && p.inline_redo) {
-                // Every warp has set its mask bits for every main tile; the producer and
-                // MMA warps wait on the same barrier, so all roles redo the same tiles.
-                __syncwarp();
-                if (lane == 0) mbar_arrive(redo_go);
-                if (__all_sync(0xffffffffu, mbar_wait(redo_go, 0, abort_flag, p.status, kStatusTimeoutEpilogue))) {
-                    for (int t = blockIdx.x, i = 0; t < tiles; t += gridDim.x, ++i) {
-                        if (!((redo_mask[i >> 5] >> (i & 31)) & 1u)) continue;
-                        int tm, tn;
-                        raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
-                        float acc[CW];
-                        if (!consume_fp32_pair<CW>(acc, pairs, lane, abort_flag, p.status)) break;
-                        if (!emit(acc, tm, tn)) break;
-                    }
-                }
-            }
+            if (!emit(acc, tm, tn, inline_redo && main_item)) break;
         }
         // peer stores become visible system-wide before the kernel is seen complete
         if (p.n_peers > 0) __threadfence_system();

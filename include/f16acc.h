@@ -181,6 +181,18 @@ int f16acc_set_sm_limit(int max_sms);
 #define F16ACC_REDO_INLINE 1
 int f16acc_set_redo_mode(int mode);
 
+/* Tile order of the chunked tcgen05 main pass, process-wide, for later calls:
+ * F16ACC_SCHEDULE_DYNAMIC (the default) launches one CTA per output tile and
+ * lets each running CTA take over the tiles of CTAs not started yet (sm_100
+ * cluster launch control), so CTAs that spend time on in-kernel redo work take
+ * fewer main tiles; F16ACC_SCHEDULE_STATIC runs one persistent CTA per SM over
+ * a fixed round-robin share.  A cap set with f16acc_set_sm_limit implies the
+ * static order.  Results are bit-identical either way.  Returns the previous
+ * order. */
+#define F16ACC_SCHEDULE_STATIC 0
+#define F16ACC_SCHEDULE_DYNAMIC 1
+int f16acc_set_schedule(int mode);
+
 /* Raw-rate probe, the B200 counterpart of the reference's bench/rate.py and
  * bench/chunkrate.py: `grid` CTAs (one per SM) each run `chunks` 32-long
  * chunks of 128x128 tcgen05 MMAs on a fixed shared-memory tile.  mode 0: MMA

@@ -104,24 +104,75 @@ def test_inline_with_bias_and_strided_output(cuda):
     check_redone(colmajor1, ws, a, b, torch.float32, bias=bias)
 
 
-@pytest.mark.parametrize("tiles_n", [32, 33], ids=["1024_tiles_per_cta", "1056_tiles_fallback"])
-def test_redo_bitmask_limit(cuda, tiles_n):
-    # one CTA: 1024 tiles fit the kernel's bitmask (the last one is bit 1023);
-    # 1056 do not, and the call falls back to the separate redo launch
-    M, N, K = 32 * 128, tiles_n * 128, 64
+@contextlib.contextmanager
+def schedule(mode):
+    lib = _lib.load()
+    prev = lib.f16acc_set_schedule(mode)
+    assert prev in (_lib.SCHEDULE_STATIC, _lib.SCHEDULE_DYNAMIC)
+    try:
+        yield
+    finally:
+        lib.f16acc_set_schedule(prev)
+
+
+def run_all_orders(a, b, out_dtype):
+    """The product under every (tile order, redo mode) pair; first = the defaults."""
+    outs = []
+    for order in (_lib.SCHEDULE_DYNAMIC, _lib.SCHEDULE_STATIC):
+        with schedule(order):
+            c1, ws1, c2, _ = both_modes(a, b, out_dtype)
+        outs += [(c1, ws1), (c2, None)]
+    return outs
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32], ids=str)
+def test_tile_orders_and_redo_modes_agree_bitwise(cuda, out_dtype):
+    # 40 x 26 tiles, more than one per SM, so the default order is dynamic
+    M, N, K = 40 * 128, 26 * 128, 256
     g = torch.Generator().manual_seed(24)
     a = torch.randn(M, K, generator=g)
     b = torch.randn(K, N, generator=g)
     a[-1] *= 300.0  # the last row block overflows against these columns
     b[:, -130:] *= 300.0
     a[:128] *= 300.0  # and the first
+    a[1000] *= 300.0
+    a, b = a.half().to(cuda), b.half().to(cuda)
+    outs = run_all_orders(a, b, out_dtype)
+    for c, _ in outs[1:]:
+        assert torch.equal(c, outs[0][0])
+    flags = check_redone(outs[0][0], outs[0][1], a, b, out_dtype)
+    assert flags[-1, -1] and flags[0, -1] and not flags.all()
+
+
+def test_one_cta_interleaves_main_and_redo_tiles(cuda):
+    # an SM cap of 1: a single persistent CTA over 1024 tiles, its redo items
+    # queued between main tiles as their flags come in
+    M, N, K = 32 * 128, 32 * 128, 64
+    g = torch.Generator().manual_seed(25)
+    a = torch.randn(M, K, generator=g)
+    b = torch.randn(K, N, generator=g)
+    a[::300] *= 300.0
+    b[:, ::700] *= 300.0
     a, b = a.half().to(cuda), b.half().to(cuda)
     with sm_limit(1):
         c1, ws1, c2, _ = both_modes(a, b, torch.float32)
     assert torch.equal(c1, c2)
     flags = check_redone(c1, ws1, a, b, torch.float32)
-    assert flags[-1, -1] and flags[0, -1] and not flags.all()
-    assert torch.isfinite(c1).all()
+    assert flags.sum() > 20 and not flags.all()
+
+
+def test_every_tile_flagged(cuda):
+    # tests/test_f16acc.py:91-101 scaled up: every chunk of every tile overflows,
+    # so every main tile queues a redo; the answer is exactly 100 everywhere
+    x = torch.full((2048, 64), 100.0, device=cuda).half()
+    w = torch.empty(2048, 64, device=cuda).half()
+    w[:, :32] = 30.0
+    w[:, 32:] = -30.0
+    w[:, 63] = -29.0
+    for c, ws in run_all_orders(x, w.t(), torch.float16):
+        assert torch.all(c == 100.0)
+        if ws is not None:
+            assert tile_flags(ws, plan(x, w.t(), _lib.VARIANT_TCGEN05)).all()
 
 
 def test_no_flags_same_as_separate(cuda):
