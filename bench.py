@@ -184,7 +184,7 @@ def run_ours(args):
     import torch
 
     from f16acc_b200 import _lib
-    from f16acc_b200.kernel import mm, mm_phase, plan, tile_flags, workspace_bytes
+    from f16acc_b200.kernel import mm, mm_ex, plan, tile_flags, workspace_bytes
     from f16acc_b200.nvml import ClockSampler
 
     world, rank, local = dist_setup(torch, want_nccl=True)
@@ -202,9 +202,9 @@ def run_ours(args):
     wss = [torch.empty(workspace_bytes(M, N, K), device=dev, dtype=torch.uint8) for _ in range(INPUT_SETS)]
 
     def one(i):
+        # one launch: the chunked main pass with its flagged tiles redone inside the kernel
         a, b = sets[i % INPUT_SETS]
-        mm_phase("main", a, b, outs[i % INPUT_SETS], wss[i % INPUT_SETS], True, variant)
-        mm_phase("redo", a, b, outs[i % INPUT_SETS], wss[i % INPUT_SETS], True, variant)
+        mm_ex(a, b, torch.float16, True, variant=variant, out=outs[i % INPUT_SETS], workspace=wss[i % INPUT_SETS])
 
     def step():
         for i in range(GEMMS_PER_STEP):
@@ -231,18 +231,16 @@ def run_ours(args):
     ms_max = max_over_ranks(torch, ms, world, dev)
     gemms_total = args.steps * GEMMS_PER_STEP * world
     value = gemms_total * flops_per_gemm() / (ms_max / 1e3) / 1e12
-    launches = args.steps * GEMMS_PER_STEP * 2
+    launches = args.steps * GEMMS_PER_STEP  # one kernel per product
 
-    # ---- roofline: main-kernel duration alone (redo still issued every product)
+    # ---- roofline: the kernel's own duration, one event pair per launch
     n_main = min(64, max(16, args.steps * 2))
     main_ms = []
     for i in range(n_main):
-        a, b = sets[i % INPUT_SETS]
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        mm_phase("main", a, b, outs[i % INPUT_SETS], wss[i % INPUT_SETS], True, variant)
+        one(i)
         e1.record(stream)
-        mm_phase("redo", a, b, outs[i % INPUT_SETS], wss[i % INPUT_SETS], True, variant)
         main_ms.append((e0, e1))
     torch.cuda.synchronize()
     main_avg_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in main_ms)
@@ -311,7 +309,7 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
             "config": {"workload": "config 2: C = A @ B, 4096^3 fp16, N(0,1)/sqrt(K)*4, B row-major, fp16 out, "
-                                   "chunked FP16 accumulate + device redo",
+                                   "chunked FP16 accumulate, flagged tiles redone in FP32 inside the same kernel",
                        "gemms_per_step": GEMMS_PER_STEP, "per_gpu": "one 4096-row M shard per product",
                        "l2": f"inputs rotate over {INPUT_SETS} (A,B) sets = {INPUT_SETS * 64} MiB > 126 MB L2",
                        "parallelism": f"dp{world} (independent M shards, no collective)",
@@ -321,7 +319,8 @@ def run_ours(args):
             "flagged_tiles": flagged,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": profiled_traffic(),
-                         "kernel": "main chunked pass", "main_kernel_ms": main_avg_ms, "peak_source": peak_src},
+                         "kernel": "tc_gemm_kernel, chunked (main pass + in-kernel redo)", "main_kernel_ms": main_avg_ms,
+                         "peak_source": peak_src},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps, "api": "f16acc_b200.mm with pinned host copies"},
