@@ -194,8 +194,7 @@ def run_ours(args):
     torch.cuda.set_device(dev)
     torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
     stream = torch.cuda.current_stream(dev)
-    variant = {"auto": _lib.VARIANT_AUTO, "tcgen05": _lib.VARIANT_TCGEN05, "mma_sync": _lib.VARIANT_MMA_SYNC}[
-        args.variant]
+    variant = {v: k for k, v in _lib.VARIANT_NAMES.items()}[args.variant]
 
     sets = make_inputs(torch, dev, seed=1 + rank, sets=INPUT_SETS)
     outs = [torch.empty(M, N, device=dev, dtype=torch.float16) for _ in range(INPUT_SETS)]
@@ -337,7 +336,7 @@ def run_ours(args):
                        "gemms_per_step": GEMMS_PER_STEP, "per_gpu": "one 4096-row M shard per product",
                        "l2": f"inputs rotate over {INPUT_SETS} (A,B) sets = {INPUT_SETS * 64} MiB > 126 MB L2",
                        "parallelism": f"dp{world} (independent M shards, no collective)",
-                       "variant": args.variant, "kernel": {1: "tcgen05", 2: "mma_sync"}.get(pl["variant"]),
+                       "variant": args.variant, "kernel": _lib.VARIANT_NAMES.get(pl["variant"]),
                        "tile": list(pl["tile"])},
             "max_rel_err_vs_fp64": max_rel,
             "flagged_tiles": flagged,
@@ -386,6 +385,17 @@ def run_workload(args):
     elif args.workload == "overflow":
         line["config"] = "config 4: 4096^3 N(0,1), 1% rows/cols x64; 4b: ~1% of tiles overflow"
         line["results"] = W.overflow(dev)
+    elif args.workload == "decode":
+        hbm = None
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                hbm = float(json.load(f)["hbm_gbs"])
+        except (OSError, KeyError, ValueError):
+            pass
+        line["config"] = ("few-row products (M = 1..64 decode tokens) on the Qwen2.5-1.5B weight shapes, "
+                          "weight [N,K], fp16 out; CUDA-graph timing over weight copies > L2")
+        line["hbm_peak_gbs"] = hbm
+        line["results"] = W.decode(dev, hbm_gbs=hbm)
     elif args.workload == "nshard":
         from f16acc_b200.kernel import mm
         from f16acc_b200.shard import nshard_mm, shard_bounds
@@ -471,7 +481,8 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--variant", choices=["auto", "tcgen05", "mma_sync"], default="auto")
-    ap.add_argument("--workload", choices=["gemm4096", "shapes", "overflow", "nshard", "prefill"], default="gemm4096",
+    ap.add_argument("--workload", choices=["gemm4096", "shapes", "overflow", "nshard", "prefill", "decode"],
+                    default="gemm4096",
                     help="gemm4096 is the headline line; the others print their own JSON line")
     ap.add_argument("--size", type=int, default=16384, help="matrix size for --workload nshard")
     ap.add_argument("--nshard-blocks", type=int, default=4, help="row blocks the sharded gather is pipelined in")

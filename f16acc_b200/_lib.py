@@ -60,7 +60,9 @@ ERR_DEVICE_TIMEOUT = 5
 ERR_TOO_LARGE = 6
 NOALLOC_MAX_TILES = 65536
 OUT_F16, OUT_F32, OUT_BF16 = 0, 1, 2
-VARIANT_AUTO, VARIANT_TCGEN05, VARIANT_MMA_SYNC = 0, 1, 2
+VARIANT_AUTO, VARIANT_TCGEN05, VARIANT_MMA_SYNC, VARIANT_SKINNY = 0, 1, 2, 3
+VARIANT_NAMES = {VARIANT_AUTO: "auto", VARIANT_TCGEN05: "tcgen05", VARIANT_MMA_SYNC: "mma_sync",
+                 VARIANT_SKINNY: "skinny"}
 REDO_SEPARATE, REDO_INLINE = 0, 1
 SCHEDULE_STATIC, SCHEDULE_DYNAMIC = 0, 1
 

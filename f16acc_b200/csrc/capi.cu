@@ -17,6 +17,7 @@
 #include "../../include/f16acc.h"
 #include "launch.h"
 #include "mma_gemm.cuh"
+#include "skinny_gemm.cuh"
 #include "tc_gemm.cuh"
 
 namespace f16acc {
@@ -136,12 +137,19 @@ std::atomic<int> g_redo_mode{F16ACC_REDO_INLINE};
 std::atomic<int> g_schedule{F16ACC_SCHEDULE_DYNAMIC};
 constexpr int kGroupM = 8;
 
-int choose_variant(const Layout& L, int64_t M, int64_t N, int64_t K, int requested) {
+// Rows up to which the few-row kernel is the automatic choice.
+constexpr int64_t kSkinnyMaxRows = 64;
+
+int choose_variant(const Layout& L, int64_t M, int64_t N, int64_t K, int requested, bool peers = false) {
     const bool dims_ok = M < (int64_t(1) << 31) && N < (int64_t(1) << 31) && K < (int64_t(1) << 31);
     const bool tc_ok = dims_ok && K > 0 && L.a_tma && (L.b_tma_k || L.b_tma_n) && encode_fn() != nullptr;
+    // cp.async wants 16-byte aligned rows with unit inner stride; no peer stores
+    const bool skinny_ok = dims_ok && K > 0 && M <= kSkinnyMaxRows && L.a_vec && (L.b_kvec || L.b_nvec) && !peers;
     if (requested == F16ACC_VARIANT_TCGEN05) return tc_ok ? F16ACC_VARIANT_TCGEN05 : -1;
     if (requested == F16ACC_VARIANT_MMA_SYNC) return dims_ok ? F16ACC_VARIANT_MMA_SYNC : -1;
+    if (requested == F16ACC_VARIANT_SKINNY) return skinny_ok ? F16ACC_VARIANT_SKINNY : -1;
     if (requested != F16ACC_VARIANT_AUTO) return -1;
+    if (skinny_ok) return F16ACC_VARIANT_SKINNY;
     if (tc_ok) return F16ACC_VARIANT_TCGEN05;
     return dims_ok ? F16ACC_VARIANT_MMA_SYNC : -1;
 }
@@ -195,7 +203,7 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
     }
     if (A == nullptr || B == nullptr) return F16ACC_ERR_INVALID_ARGUMENT;
     const Layout L = analyse(A, sAm, sAk, B, sBk, sBn, M, N, K);
-    int v = choose_variant(L, M, N, K, variant);
+    int v = choose_variant(L, M, N, K, variant, n_peers > 0);
     if (v < 0) return variant == F16ACC_VARIANT_AUTO ? F16ACC_ERR_INVALID_ARGUMENT : F16ACC_ERR_UNSUPPORTED;
     if (chunked) {
         if (workspace == nullptr || ws_bytes < f16acc_workspace_bytes(M, N, K) ||
@@ -204,6 +212,38 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
     }
     const int esize = c_dtype == F16ACC_OUT_F32 ? 4 : 2;
     const uintptr_t pc = reinterpret_cast<uintptr_t>(C);
+
+    if (v == F16ACC_VARIANT_SKINNY) {
+        SkinnyParams s;
+        std::memset(&s, 0, sizeof(s));
+        s.A = static_cast<const __half*>(A);
+        s.B = static_cast<const __half*>(B);
+        s.C = C;
+        s.sAm = L.sAm;
+        s.sBk = L.sBk;
+        s.sBn = L.sBn;
+        s.sCm = sCm;
+        s.sCn = sCn;
+        s.M = int(M);
+        s.N = int(N);
+        s.K = int(K);
+        int splits = 1, kper = 64;
+        skinny_split(N, K, &splits, &kper);
+        s.kper = kper;
+        s.c_vec = (sCn == 1 && pc % (4 * esize) == 0 && sCm % 4 == 0) ? 1 : 0;
+        s.flags = static_cast<uint8_t*>(workspace);
+        s.bias = static_cast<const __half*>(bias);
+        s.sbias = sbias;
+        s.inline_redo = chunked && phases == kPhaseBoth &&
+                        g_redo_mode.load(std::memory_order_relaxed) == F16ACC_REDO_INLINE;
+        const bool b_kn = !L.b_kvec;  // N-contiguous B
+        if ((phases & kPhaseMain) && launch_skinny(s, chunked != 0, b_kn, c_dtype, false, splits, stream) != cudaSuccess)
+            return F16ACC_ERR_CUDA;
+        if (chunked && (phases & kPhaseRedo) && !s.inline_redo &&
+            launch_skinny(s, false, b_kn, c_dtype, true, splits, stream) != cudaSuccess)
+            return F16ACC_ERR_CUDA;
+        return F16ACC_OK;
+    }
 
     TcParams p;
     std::memset(&p, 0, sizeof(p));
@@ -384,8 +424,8 @@ int f16acc_get_plan(const void* A, int64_t sAm, int64_t sAk, const void* B, int6
     const int v = choose_variant(L, M, N, K, variant);
     if (v < 0) return variant == F16ACC_VARIANT_AUTO ? F16ACC_ERR_INVALID_ARGUMENT : F16ACC_ERR_UNSUPPORTED;
     out->variant = v;
-    out->tile_m = 128;
-    out->tile_n = v == F16ACC_VARIANT_TCGEN05 ? tc_shape().bn : MmaCfg::BN;
+    out->tile_m = v == F16ACC_VARIANT_SKINNY ? skinny_rows(M) : 128;
+    out->tile_n = v == F16ACC_VARIANT_TCGEN05 ? tc_shape().bn : (v == F16ACC_VARIANT_SKINNY ? SkinnyCfg::BN : MmaCfg::BN);
     out->tiles_m = cdiv(M, out->tile_m);
     out->tiles_n = cdiv(N, out->tile_n);
     return F16ACC_OK;

@@ -26,6 +26,16 @@ cudaError_t launch_tc(const TcParams& p, TcShape shape, bool chunked, bool b_mn,
 // mma.sync kernel: a_mode / b_mode from LoadMode.
 cudaError_t launch_mma(const MmaParams& p, bool chunked, int a_mode, int b_mode, int out, bool redo, int grid,
                        cudaStream_t stream);
+// Few-row kernel (M <= 64): grid (ceil(N / 128), splits) in clusters of
+// `splits` CTAs along K.  skinny_rows: the padded row count (16, 32 or 64)
+// for M; skinny_split: the K split of a shape (a function of N and K only, so
+// every pass over the same shape adds its partial sums in the same order).
+struct SkinnyParams;
+int skinny_rows(int64_t M);
+void skinny_split(int64_t N, int64_t K, int* splits, int* kper);
+cudaError_t launch_skinny(const SkinnyParams& p, bool chunked, bool b_kn, int out, bool redo, int splits,
+                          cudaStream_t stream);
+
 // K = 0: C = 0, or C[r][c] = bias[c] when a bias is given.
 cudaError_t launch_fill_zero(void* C, int64_t sCm, int64_t sCn, int M, int N, int out, cudaStream_t stream,
                              const __half* bias = nullptr, int64_t sbias = 0);
@@ -34,6 +44,13 @@ cudaError_t launch_fill_zero(void* C, int64_t sCm, int64_t sCn, int M, int N, in
 // mode 2 the chunk pipeline; `out` holds grid * (64 + 128 * epi_split) floats.
 cudaError_t launch_chunk_rate(int mode, int epi_split, int chunks, int grid, float* out, int* status,
                               cudaStream_t stream);
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per kernel and device.
+cudaError_t ensure_smem_attr_raw(const void* kernel, int smem);
+template <typename Kernel>
+cudaError_t ensure_smem_attr(Kernel kernel, int smem) {
+    return ensure_smem_attr_raw(reinterpret_cast<const void*>(kernel), smem);
+}
 
 // Launch helper: cudaLaunchKernelEx with optional programmatic stream
 // serialisation (the dependent kernel may start its prologue while the

@@ -9,23 +9,22 @@
 namespace f16acc {
 
 namespace {
-
-// cudaFuncSetAttribute is per function and device; do it once for each pair.
 std::mutex g_attr_mu;
 std::set<std::pair<const void*, int>> g_attr_done;
+}  // namespace
 
-template <typename Kernel>
-cudaError_t ensure_smem_attr(Kernel kernel, int smem) {
+cudaError_t ensure_smem_attr_raw(const void* kernel, int smem) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    const void* key = reinterpret_cast<const void*>(kernel);
     std::lock_guard<std::mutex> lock(g_attr_mu);
-    if (g_attr_done.count({key, dev})) return cudaSuccess;
+    if (g_attr_done.count({kernel, dev})) return cudaSuccess;
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e == cudaSuccess) g_attr_done.insert({key, dev});
+    if (e == cudaSuccess) g_attr_done.insert({kernel, dev});
     return e;
 }
+
+namespace {
 
 template <int BN, int EPI, bool CHUNKED, bool B_MN, int OUT, bool REDO>
 cudaError_t launch_one(const TcParams& p, int grid, cudaStream_t stream) {

@@ -26,7 +26,7 @@ def main(argv=None) -> int:
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--layout", choices=["row_major", "w_t"], default="row_major")
-    ap.add_argument("--variant", choices=["auto", "tcgen05", "mma_sync"], default="auto")
+    ap.add_argument("--variant", choices=["auto", "tcgen05", "mma_sync", "skinny"], default="auto")
     ap.add_argument("--fp32-acc", action="store_true", help="chunked=False (plain FP32 accumulation)")
     ap.add_argument("--out", choices=["f16", "f32"], default="f16")
     ap.add_argument("--reps", type=int, default=10)
@@ -45,7 +45,7 @@ def main(argv=None) -> int:
         B = (torch.randn(a.k, a.n, device=dev, generator=g) * scale).half()
     else:
         B = (torch.randn(a.n, a.k, device=dev, generator=g) * scale).half().t()
-    variant = {"auto": _lib.VARIANT_AUTO, "tcgen05": _lib.VARIANT_TCGEN05, "mma_sync": _lib.VARIANT_MMA_SYNC}[a.variant]
+    variant = {v: k for k, v in _lib.VARIANT_NAMES.items()}[a.variant]
     out_dtype = torch.float16 if a.out == "f16" else torch.float32
     chunked = not a.fp32_acc
     C, ws = mm_ex(A, B, out_dtype, chunked, variant=variant)
@@ -61,7 +61,7 @@ def main(argv=None) -> int:
     ms = [e0.elapsed_time(e1) for e0, e1 in times]
     med = statistics.median(ms)
     res = {"m": a.m, "n": a.n, "k": a.k, "layout": a.layout, "chunked": chunked, "out": a.out,
-           "variant": {1: "tcgen05", 2: "mma_sync"}[plan(A, B, variant)["variant"]],
+           "variant": _lib.VARIANT_NAMES[plan(A, B, variant)["variant"]],
            "median_ms": med, "tflops": 2.0 * a.m * a.n * a.k / (med / 1e3) / 1e12}
     if a.check:
         ref = A.double() @ B.double()

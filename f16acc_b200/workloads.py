@@ -82,7 +82,60 @@ def shapes(device, reps: int = 20, M: int = 2048, seed: int = 2):
         out.append({"shape": name, "M": M, "K": K, "N": N, "ours_tflops": flops / t_ours / 1e9,
                     "cublas_f32acc_tflops": flops / t_cublas / 1e9, "speedup_vs_cublas": t_cublas / t_ours,
                     "ours_ms": t_ours, "ours_gbs": bytes_alg / t_ours / 1e6, "max_rel_err_vs_fp64": err,
-                    "kernel": {1: "tcgen05", 2: "mma_sync"}[plan(x, w.t())["variant"]]})
+                    "kernel": _lib.VARIANT_NAMES[plan(x, w.t())["variant"]]})
+    return out
+
+
+# ---------------------------------------------------------------- few rows (decode shapes)
+def graph_time(fns) -> float:
+    """Per-call device milliseconds of the calls in `fns` replayed from one CUDA
+    graph (no host launch overhead in the number)."""
+    for f in fns:
+        f()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for f in fns:
+            f()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(3):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / (3 * len(fns))
+
+
+def decode(device, rows=(1, 16, 32, 64), hbm_gbs: float | None = None, calls: int = 24, seed: int = 5):
+    """Few-row products (M = batch of decode tokens) on the Qwen2.5-1.5B weight
+    shapes: the few-row kernel against the tcgen05 kernel and cuBLAS, in GB/s
+    of algorithmic bytes (A + B + C) and as a fraction of the HBM peak.  Each
+    timing replays `calls` products over weight copies that together exceed L2."""
+    torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = []
+    for M in rows:
+        for name, K, N in QWEN_SHAPES:
+            copies = max(1, min(calls, (300 << 20) // (2 * K * N) + 1))
+            ws = [(torch.randn(N, K, device=device, generator=g) * 0.02).half() for _ in range(copies)]
+            x = torch.randn(M, K, device=device, generator=g).half()
+            byts = 2 * (M * K + K * N + M * N)
+            res = {"shape": name, "M": M, "K": K, "N": N, "kernel": _lib.VARIANT_NAMES[plan(x, ws[0].t())["variant"]]}
+            arms = (("f16acc", lambda w: (lambda: mm(x, w.t()))),
+                    ("f16acc_tcgen05", lambda w: (lambda: mm_ex(x, w.t(), variant=_lib.VARIANT_TCGEN05))),
+                    ("cublas", lambda w: (lambda: torch.nn.functional.linear(x, w))))
+            for arm, make in arms:
+                ms = graph_time([make(ws[i % copies]) for i in range(calls)])
+                res[arm + "_us"] = ms * 1e3
+                res[arm + "_gbs"] = byts / (ms / 1e3) / 1e9
+                if hbm_gbs:
+                    res[arm + "_frac_hbm"] = res[arm + "_gbs"] / hbm_gbs
+            c = mm(x, ws[0].t())
+            res["max_rel_err_vs_fp64"] = rel(c, x.double() @ ws[0].double().t())
+            out.append(res)
+            del ws
     return out
 
 
