@@ -21,6 +21,7 @@ enum DeviceStatus : int {
     kStatusTimeoutProbe = 0x104,      // a probe kernel's wait ran out
     kStatusTimeoutSchedule = 0x105,   // the tile scheduler waited too long for the epilogue's flag decisions
     kStatusRedoQueueFull = 0x106,     // in-kernel redo queue overflow (a bug; the kernel stops)
+    kStatusTimeoutStore = 0x107,      // store warps waited too long for a staged tile
 };
 
 // A wait gives up after this many nanoseconds of %globaltimer.  The longest

@@ -80,13 +80,22 @@ struct alignas(16) TcCtrl {
     uint64_t full[STAGES], empty[STAGES];
     uint64_t tfull[NBUF], tempty[NBUF];
     uint64_t sched_full[kSchedDepth], sched_empty[kSchedDepth];
-    uint64_t clc_bar, drain, epi_bar;
+    uint64_t st_full[2], st_empty[2];  // staging tile b: staged by the epilogue / copied out by the store warps
+    int4 st_meta[2];                   // {tm, tn, TcStore kind, 0} of the tile in staging b
+    uint64_t clc_bar, drain;
     uint32_t tmem_slot;
     int abort_flag;
-    int rq_tail;                       // redo items pushed (epilogue)
+    int rq_tail;                       // redo items pushed (store warps)
     int rq_head;                       // redo items taken (producer)
-    int main_done;                     // main tiles whose flag is decided (epilogue)
-    int tile_bad[2];                   // per-tile OR of the warps' flags, double-buffered
+    int main_done;                     // main tiles whose flag is decided (store warps)
+    int tile_bad[2];                   // OR of the epilogue warps' flags for the tile in staging b
+};
+
+// What a staged tile asks of the store warps.
+enum TcStore : int {
+    kStoreTile = 0,     // copy it out
+    kStoreDecide = 1,   // copy it out, and decide whether it needs the in-kernel FP32 redo
+    kStoreEnd = 2,      // no tile: the epilogue is done
 };
 
 template <int BN_, int EPI_SPLIT_, int OUT_>
@@ -96,8 +105,9 @@ struct TcConfig {
     static constexpr int BK = 64;  // one 128-byte swizzle row of f16 = two 32-long chunks
     static constexpr int EPI_SPLIT = EPI_SPLIT_;
     static constexpr int EPI_WARPS = 4 * EPI_SPLIT;
+    static constexpr int STORE_WARPS = 2;       // copy staged tiles out to C (and peers)
     static constexpr int CW = BN / EPI_SPLIT;  // columns per epilogue warp
-    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int THREADS = 64 + 32 * (EPI_WARPS + STORE_WARPS);
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -105,14 +115,18 @@ struct TcConfig {
     // Output staging: the finished tile is assembled in smem so rows leave in
     // whole, coalesced 16-byte-per-lane stores (local C and every peer).  Row
     // pitch padded by 16 bytes so the per-thread row writes spread over banks.
+    // Two staging tiles let the epilogue stage tile k+1 while the store warps
+    // copy tile k out; an fp32 tile is twice the size and gets one.
     static constexpr int STAGE_PITCH = BN * OUT_BYTES + 16;
     static constexpr int STAGING_BYTES = BM * STAGE_PITCH;
-    static constexpr int STAGES = OUT_BYTES == 4 ? 4 : 5;
+    static constexpr int SBUF = OUT_BYTES == 4 ? 1 : 2;
+    static constexpr int STAGES = 4;  // measured: a fifth stage adds nothing to either mode
     static constexpr int TMEM_COLS = 512;
     static constexpr int ACC_COLS = BN;  // one 32-bit TMEM column per accumulator element, f16 or f32
     static constexpr int NBUF = TMEM_COLS / ACC_COLS;
     using Ctrl = TcCtrl<STAGES, NBUF>;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*alignment slack*/ + int(sizeof(Ctrl));
+    static constexpr int SMEM_BYTES =
+        STAGES * STAGE_BYTES + SBUF * STAGING_BYTES + 1024 /*alignment slack*/ + int(sizeof(Ctrl));
     static constexpr int FLAG_BYTES_PER_WARP = kFlagBytesPerTile / EPI_WARPS;  // every slot byte gets written
     static_assert(FLAG_BYTES_PER_WARP * EPI_WARPS == kFlagBytesPerTile &&
                       (FLAG_BYTES_PER_WARP == 1 || FLAG_BYTES_PER_WARP == 2),
@@ -191,13 +205,12 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
     uint8_t* staging = smem + STAGES * Cfg::STAGE_BYTES;
-    auto* ctrl = reinterpret_cast<typename Cfg::Ctrl*>(staging + Cfg::STAGING_BYTES);
+    auto* ctrl = reinterpret_cast<typename Cfg::Ctrl*>(staging + Cfg::SBUF * Cfg::STAGING_BYTES);
     uint64_t* full = ctrl->full;
     uint64_t* empty = ctrl->empty;
     uint64_t* tfull = ctrl->tfull;
     uint64_t* tempty = ctrl->tempty;
     uint64_t* drain = &ctrl->drain;
-    uint64_t* epi_bar = &ctrl->epi_bar;  // epilogue warps meet here around the staged store
     volatile int* abort_flag = &ctrl->abort_flag;
     volatile int* rq_tail = &ctrl->rq_tail;
     volatile int* rq_head = &ctrl->rq_head;
@@ -221,7 +234,10 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
         }
         mbar_init(&ctrl->clc_bar, 1);
         mbar_init(drain, 1);
-        mbar_init(epi_bar, Cfg::EPI_WARPS);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&ctrl->st_full[b], Cfg::EPI_WARPS);
+            mbar_init(&ctrl->st_empty[b], Cfg::STORE_WARPS);
+        }
         *abort_flag = 0;
         *rq_tail = 0;
         *rq_head = 0;
@@ -456,72 +472,33 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
             umma_commit(drain);
             mbar_wait_drain(drain, 0);
         }
-    } else {
+    } else if (warp < 2 + Cfg::EPI_WARPS) {
         // ------------------------------------------------------------ epilogue
         const int e = warp - 2;          // epilogue warp index
         const int q = warp & 3;          // TMEM lane quarter this warp may access
         const int colg = e >> 2;         // column slice
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-        void* dsts[1 + kMaxPeers] = {p.C};  // this GPU's C, then the peers' copies
-        for (int i = 0; i < p.n_peers; ++i) dsts[1 + i] = p.peers[i];
-        uint32_t epi_phase = 0;
         ChunkRing<NBUF> ring{tfull, tempty, tmem + lane_base + colg * CW, Cfg::ACC_COLS};    // FP32 mode
         PairRing<CW> pairs{tfull, tempty, tmem + lane_base + colg * CW, Cfg::ACC_COLS};     // chunked mode
-        // Stage the tile in smem (rounded to the output type), then copy it out to C
-        // and to every peer's buffer (fused all-gather): whole rows in coalesced
-        // 16-byte-per-lane stores when C allows, else element by element.  The bias
-        // (after the flag: the reference adds it outside the kernel) goes on in the
-        // copy-out, to the product already rounded to the output type.  False when
-        // a wait gave up.
-        //
-        // `decide` (a main tile of the chunked kernel with the in-kernel redo):
-        // once every warp has passed the first barrier its flag is in
-        // tile_bad[par]; epilogue warp 0 queues the tile for its FP32 redo if any
-        // warp saw a non-finite value, then counts the tile as decided.
-        uint32_t par = 0;
-        int decided = 0;
-        auto emit = [&](const float (&acc)[CW], int tm, int tn, bool decide) -> bool {
-            stage_row<OUT, CW, Cfg::STAGE_PITCH>(staging, q * 32 + lane, colg * CW, acc);
+        // Finished tiles go to the store warps through the staging tiles, in order:
+        // tile k in staging k % SBUF.  take_staging waits until the store warps have
+        // copied out that buffer's previous tile; hand_over passes the staged tile
+        // (or the end marker) on.  The epilogue itself never waits for the copy-out.
+        int handed = 0;
+        auto take_staging = [&]() -> bool {
+            const uint32_t par = (uint32_t(handed) / Cfg::SBUF) & 1u;
+            return __all_sync(0xffffffffu, mbar_wait(&ctrl->st_empty[handed % Cfg::SBUF], par ^ 1u, abort_flag,
+                                                     p.status, kStatusTimeoutEpilogue));
+        };
+        auto hand_over = [&](int tm, int tn, int kind) {
+            const int b = handed % Cfg::SBUF;
+            if (e == 0 && lane == 0) ctrl->st_meta[b] = make_int4(tm, tn, kind, 0);
             __syncwarp();
-            if (lane == 0) mbar_arrive(epi_bar);
-            if (!__all_sync(0xffffffffu,
-                            mbar_wait(epi_bar, epi_phase, abort_flag, p.status, kStatusTimeoutEpilogue)))
-                return false;
-            epi_phase ^= 1u;
-            if (decide) {
-                if (e == 0 && lane == 0) {
-                    if (atomicExch(&ctrl->tile_bad[par], 0) != 0) {
-                        const int tail = *rq_tail;
-                        if (tail - *rq_head >= kRedoQueue) {
-                            atomicCAS(p.status, 0, kStatusRedoQueueFull);
-                            *abort_flag = 1;
-                        } else {
-                            ctrl->redo_q[tail % kRedoQueue] = make_int2(tm, tn);
-                            __threadfence_block();
-                            *rq_tail = tail + 1;
-                        }
-                    }
-                    __threadfence_block();
-                    *main_done = ++decided;
-                }
-                par ^= 1u;
-            }
-            if (p.c_vec)
-                store_staged<OUT, BM, BN, Cfg::STAGE_PITCH, Cfg::EPI_WARPS>(
-                    staging, dsts, 1 + p.n_peers, p.sCm, tm * BM, tn * BN, p.M, p.N, e, lane, p.bias, p.sbias);
-            else
-                store_staged_strided<OUT, BM, BN, Cfg::STAGE_PITCH, Cfg::EPI_WARPS>(
-                    staging, dsts, 1 + p.n_peers, p.sCm, p.sCn, tm * BM, tn * BN, p.M, p.N, e, lane, p.bias,
-                    p.sbias);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(epi_bar);  // staging free again once every warp has copied out
-            if (!__all_sync(0xffffffffu,
-                            mbar_wait(epi_bar, epi_phase, abort_flag, p.status, kStatusTimeoutEpilogue)))
-                return false;
-            epi_phase ^= 1u;
-            return true;
+            if (lane == 0) mbar_arrive(&ctrl->st_full[b]);
+            ++handed;
         };
         const bool inline_redo = CHUNKED && p.inline_redo != 0;
+        bool finished = false;  // left the loop at the end item (not by giving up on a wait)
         for (uint32_t qi = 0, qph = 0;;) {
             if (!__all_sync(0xffffffffu,
                             mbar_wait(&ctrl->sched_full[qi], qph, abort_flag, p.status, kStatusTimeoutEpilogue)))
@@ -530,10 +507,14 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&ctrl->sched_empty[qi]);
             if (++qi == kSchedDepth) { qi = 0; qph ^= 1u; }
-            if (w.z == kWorkEnd) break;
+            if (w.z == kWorkEnd) {
+                finished = true;
+                break;
+            }
             const int tm = w.x, tn = w.y;
             const bool main_item = w.z == kWorkMain;
             float acc[CW];
+            bool bad = false;
             if constexpr (CHUNKED) {
                 if (main_item) {
 #pragma unroll
@@ -542,14 +523,13 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
                     float z = 0.0f;
 #pragma unroll
                     for (int j = 0; j < CW; ++j) z = nonfinite_probe(z, acc[j]);
-                    const bool bad = __any_sync(0xffffffffu, z != z);
+                    bad = __any_sync(0xffffffffu, z != z);
                     if (lane == 0) {
                         uint8_t* slot = p.flags + (static_cast<int64_t>(tm) * p.tiles_n + tn) * kFlagBytesPerTile;
                         if constexpr (Cfg::FLAG_BYTES_PER_WARP == 2)
                             *reinterpret_cast<uint16_t*>(slot + 2 * e) = bad ? 1 : 0;
                         else
                             slot[e] = bad ? 1 : 0;
-                        if (bad && inline_redo) atomicOr(&ctrl->tile_bad[par], 1);
                     }
                 } else {
                     if (!consume_fp32_pair<CW>(acc, pairs, lane, abort_flag, p.status)) break;
@@ -567,7 +547,62 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
                 }
                 ring.release(lane);
             }
-            if (!emit(acc, tm, tn, inline_redo && main_item)) break;
+            // Stage the tile, rounded to the output type, for the store warps.
+            if (!take_staging()) break;
+            const int b = handed % Cfg::SBUF;
+            stage_row<OUT, CW, Cfg::STAGE_PITCH>(staging + b * Cfg::STAGING_BYTES, q * 32 + lane, colg * CW, acc);
+            const bool decide = inline_redo && main_item;
+            if (decide && bad && lane == 0) atomicOr(&ctrl->tile_bad[b], 1);
+            hand_over(tm, tn, decide ? kStoreDecide : kStoreTile);
+        }
+        if (finished && take_staging()) hand_over(0, 0, kStoreEnd);
+    } else {
+        // ------------------------------------------------------------ store warps
+        // Copy each staged tile out to C and to every peer's buffer (fused
+        // all-gather): whole rows in coalesced 16-byte-per-lane stores when C
+        // allows, else element by element.  The bias (after the flag: the
+        // reference adds it outside the kernel) goes on here, to the product
+        // already rounded to the output type.  For a main tile of the chunked
+        // kernel with the in-kernel redo, store warp 0 reads the OR of the 16
+        // epilogue warps' flags, queues the tile for its FP32 redo if it is set,
+        // and counts the tile as decided for the scheduler.
+        const int sw = warp - 2 - Cfg::EPI_WARPS;
+        void* dsts[1 + kMaxPeers] = {p.C};  // this GPU's C, then the peers' copies
+        for (int i = 0; i < p.n_peers; ++i) dsts[1 + i] = p.peers[i];
+        int decided = 0;
+        for (int k = 0;; ++k) {
+            const int b = k % Cfg::SBUF;
+            const uint32_t par = (uint32_t(k) / Cfg::SBUF) & 1u;
+            if (!__all_sync(0xffffffffu,
+                            mbar_wait(&ctrl->st_full[b], par, abort_flag, p.status, kStatusTimeoutStore)))
+                break;
+            const int4 m = ctrl->st_meta[b];
+            if (m.z == kStoreEnd) break;
+            const int tm = m.x, tn = m.y;
+            if (m.z == kStoreDecide && sw == 0 && lane == 0) {
+                if (atomicExch(&ctrl->tile_bad[b], 0) != 0) {
+                    const int tail = *rq_tail;
+                    if (tail - *rq_head >= kRedoQueue) {
+                        atomicCAS(p.status, 0, kStatusRedoQueueFull);
+                        *abort_flag = 1;
+                    } else {
+                        ctrl->redo_q[tail % kRedoQueue] = make_int2(tm, tn);
+                        __threadfence_block();
+                        *rq_tail = tail + 1;
+                    }
+                }
+                __threadfence_block();
+                *main_done = ++decided;
+            }
+            const uint8_t* stg = staging + b * Cfg::STAGING_BYTES;
+            if (p.c_vec)
+                store_staged<OUT, BM, BN, Cfg::STAGE_PITCH, Cfg::STORE_WARPS>(
+                    stg, dsts, 1 + p.n_peers, p.sCm, tm * BM, tn * BN, p.M, p.N, sw, lane, p.bias, p.sbias);
+            else
+                store_staged_strided<OUT, BM, BN, Cfg::STAGE_PITCH, Cfg::STORE_WARPS>(
+                    stg, dsts, 1 + p.n_peers, p.sCm, p.sCn, tm * BM, tn * BN, p.M, p.N, sw, lane, p.bias, p.sbias);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctrl->st_empty[b]);  // the staging tile is free again
         }
         // peer stores become visible system-wide before the kernel is seen complete
         if (p.n_peers > 0) __threadfence_system();
