@@ -448,6 +448,21 @@ int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void*
                : F16ACC_ERR_CUDA;
 }
 
+int f16acc_probe_pair_trace(int variant, int epi_split, int npairs, int grid, void* events, void* out, int device,
+                            void* stream) {
+    if (variant < 0 || variant > 2 || (epi_split != 2 && epi_split != 4) || npairs < 4 || grid <= 0 ||
+        events == nullptr || out == nullptr)
+        return F16ACC_ERR_INVALID_ARGUMENT;
+    DeviceInfo* info = device_info(device);
+    if (!info) return F16ACC_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess || info->err != cudaSuccess) return F16ACC_ERR_CUDA;
+    return launch_pair_trace(variant, epi_split, npairs, grid, static_cast<long long*>(events),
+                             static_cast<float*>(out), info->status, static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? F16ACC_OK
+               : F16ACC_ERR_CUDA;
+}
+
 int f16acc_set_sm_limit(int max_sms) {
     if (max_sms < 0) return F16ACC_ERR_INVALID_ARGUMENT;
     const int prev = g_sm_limit.exchange(max_sms);

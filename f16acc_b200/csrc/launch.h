@@ -52,6 +52,11 @@ cudaError_t ensure_smem_attr(Kernel kernel, int smem) {
     return ensure_smem_attr_raw(reinterpret_cast<const void*>(kernel), smem);
 }
 
+// Timed pair pipeline (trace_probe.cu): `ev` holds npairs x 9 SM-clock stamps
+// from CTA 0, `out` grid * (64 + 128 * epi_split) floats.
+cudaError_t launch_pair_trace(int variant, int epi_split, int npairs, int grid, long long* ev, float* out,
+                              int* status, cudaStream_t stream);
+
 // Launch helper: cudaLaunchKernelEx with optional programmatic stream
 // serialisation (the dependent kernel may start its prologue while the
 // previous kernel on the stream drains; it calls griddepcontrol.wait before

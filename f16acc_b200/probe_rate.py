@@ -52,12 +52,50 @@ def run(mode: int, epi_split: int, chunks: int, reps: int, dev: torch.device):
     return sms, med, flops / (med / 1e3) / 1e12, clocks.summary()
 
 
+def trace(dev: torch.device, npairs: int = 2048) -> int:
+    """The timed pair hand-off: median SM cycles of each step per pair (pairs
+    npairs/10 .. 9*npairs/10 of CTA 0, all 148 CTAs running)."""
+    lib = _lib.load()
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    names = ("pipeline", "pipeline_without_adds", "mma_warp_alone")
+    for epi in (4, 2):
+        for variant in (0, 1, 2):
+            ev = torch.zeros(npairs * 9, dtype=torch.int64, device=dev)
+            out = torch.empty(sms * (64 + 128 * epi), device=dev)
+            for _ in range(3):  # the last run's stamps are read
+                rc = lib.f16acc_probe_pair_trace(variant, epi, npairs, sms, ev.data_ptr(), out.data_ptr(),
+                                                 dev.index or 0, torch.cuda.current_stream(dev).cuda_stream)
+                if rc != 0:
+                    raise RuntimeError(_lib.strerror(rc))
+            torch.cuda.synchronize()
+            e = ev.view(npairs, 9).cpu().tolist()
+            rows = range(npairs // 10, npairs * 9 // 10)
+            med = lambda f: statistics.median(f(i) for i in rows)  # noqa: E731
+            res = {"probe": "pair_trace_" + names[variant], "epilogue_warps": 4 * epi,
+                   "pair_period": med(lambda i: e[i + 1][4] - e[i][4]),
+                   "mma_fence": med(lambda i: e[i][1] - e[i][0]),
+                   "mma_first_issue": med(lambda i: e[i][2] - e[i][1]),
+                   "mma_next_three_issue": med(lambda i: e[i][3] - e[i][2]),
+                   "mma_commit_issue": med(lambda i: e[i][4] - e[i][3])}
+            if variant != 2:
+                last = lambda i: max(e[i][6], e[i][8])  # noqa: E731
+                res.update({"commit_to_epilogue_wake": med(lambda i: e[i][5] - e[i][4]),
+                            "epilogue_wake_to_release": med(lambda i: e[i][6] - e[i][5]),
+                            "release_to_mma_wake": med(lambda i: e[i + 2][0] - last(i) if i + 2 < npairs else 0)})
+            res["frac_of_peak"] = 256.0 / res["pair_period"]  # 4 MMAs of 64 cycles per pair
+            print(json.dumps(res), flush=True)
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--chunks", type=int, default=4096)
     ap.add_argument("--reps", type=int, default=5)
+    ap.add_argument("--trace", action="store_true", help="only the timed pair hand-off (per-step SM cycles)")
     a = ap.parse_args(argv)
     dev = torch.device("cuda:0")
+    if a.trace:
+        return trace(dev)
     probes = [("mma_f16acc", 0, 2), ("mma_f32acc", 1, 2), ("chunk_pipeline_8warp", 2, 2),
               ("chunk_pipeline_16warp", 2, 4), ("pipeline_no_adds_8warp", 3, 2), ("pipeline_no_adds_16warp", 3, 4),
               ("handoff_only_8warp", 4, 2), ("tmem_ld_only_8warp", 6, 2), ("tmem_ld_only_16warp", 6, 4),

@@ -229,6 +229,18 @@ int f16acc_set_schedule(int mode);
  * Asynchronous on `stream`; time it with events. */
 int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void *out, int device, void *stream);
 
+/* Timed chunk-pair hand-off (a measurement tool): the pair pipeline of the
+ * chunked kernel without global operands, `npairs` pairs on `grid` CTAs of
+ * 2 + 4*epi_split warps, with SM-clock stamps of every step written by CTA 0
+ * to `events` (device memory, npairs x 9 int64: MMA warp woke, after its
+ * fence, first MMA issued, fourth MMA issued, commit issued, epilogue warp 0
+ * woke and released, last epilogue warp woke and released).  variant 0 = the
+ * product's hand-off, 1 = without the FP32 adds, 2 = the MMA warp alone
+ * (no waits; only its five stamps are written).  `out` holds
+ * grid * (64 + 128*epi_split) floats. */
+int f16acc_probe_pair_trace(int variant, int epi_split, int npairs, int grid, void *events, void *out, int device,
+                            void *stream);
+
 /* Device status word: 0, or the code of the first wait a kernel on `device`
  * gave up on since the last reset.  Synchronises the device.  reset != 0
  * clears it.  Returns -1 when the status cannot be read. */
