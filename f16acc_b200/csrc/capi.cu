@@ -450,7 +450,7 @@ int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void*
 
 int f16acc_probe_pair_trace(int variant, int epi_split, int npairs, int grid, void* events, void* out, int device,
                             void* stream) {
-    if (variant < 0 || variant > 2 || (epi_split != 2 && epi_split != 4) || npairs < 4 || grid <= 0 ||
+    if (variant < 0 || variant > 3 || (epi_split != 2 && epi_split != 4) || npairs < 4 || grid <= 0 ||
         events == nullptr || out == nullptr)
         return F16ACC_ERR_INVALID_ARGUMENT;
     DeviceInfo* info = device_info(device);

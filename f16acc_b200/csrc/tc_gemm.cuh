@@ -10,21 +10,24 @@
 //   f16acc/kernel.py:70-71  tile flag = any accumulator not finite.
 //   f16acc/kernel.py:75-81  redo: flagged tiles recomputed in FP32 mode.
 //
-// Design (one persistent CTA per SM, 128 x BN output tile, 1-CTA UMMA):
-//   warp 0      TMA producer: A [128 x 64] and B [BN x 64] (or [64 x BN] when B
-//               is N-contiguous) per stage into a STAGES-deep smem ring,
-//               128-byte swizzle, completion counted on full[s].
-//   warp 1      TMEM owner + MMA issuer (one lane).  Chunked mode: per 32-long
-//               chunk, two K=16 tcgen05.mma kind::f16 with an FP16 D into one
-//               of NBUF TMEM buffers (first with accumulate off), then
-//               tcgen05.commit -> tfull[b].  FP32 mode: the whole K loop into
-//               one FP32 TMEM buffer per tile.
-//   warps 2..   epilogue, 4*EPI_SPLIT warps: warp w reads TMEM lanes
+// Design (128 x BN output tiles, 1-CTA UMMA, one CTA per SM at a time):
+//   warp 0      tile scheduler and TMA producer: A [128 x 64] and B [BN x 64]
+//               (or [64 x BN] when B is N-contiguous) per stage into a 4-stage
+//               smem ring, 128-byte swizzle, completion counted on full[s].
+//   warps 1-2   MMA issuers (one lane each; warp 1 owns TMEM).  Chunked mode:
+//               per 64-wide stage, the two 32-long chunks go to the two chunk
+//               buffers of a pair, warp 1 issuing chunk 0's two K=16
+//               tcgen05.mma kind::f16 (FP16 D, first with accumulate off) and
+//               warp 2 chunk 1's, each then tcgen05.commit -> tfull[pair].
+//               FP32 mode: warp 1 alone, the whole K loop into one FP32 buffer.
+//   warps 3..   epilogue, 4*EPI_SPLIT warps: warp w reads TMEM lanes
 //               32*(w%4).. (its lane quarter) and a CW = BN/EPI_SPLIT column
-//               slice.  Chunked mode: per chunk tcgen05.ld (FP16 pairs packed),
-//               release the buffer, then one mixed-precision FP32 add per
+//               slice.  Chunked mode: per pair tcgen05.ld (FP16 pairs packed),
+//               release the buffers, then one mixed-precision FP32 add per
 //               element into register accumulators; at tile end a non-finite
-//               probe sets the tile's flag slot and the row slice is stored.
+//               probe sets the tile's flag bytes and the tile is staged in smem.
+//   last warp   store warp: copies each staged tile out to C (and the peers)
+//               and makes the in-kernel redo decisions.
 // No cluster multicast anywhere; every load reads this GPU's own memory.
 #pragma once
 
@@ -105,9 +108,15 @@ struct TcConfig {
     static constexpr int BK = 64;  // one 128-byte swizzle row of f16 = two 32-long chunks
     static constexpr int EPI_SPLIT = EPI_SPLIT_;
     static constexpr int EPI_WARPS = 4 * EPI_SPLIT;
-    static constexpr int STORE_WARPS = 2;       // copy staged tiles out to C (and peers)
+    static constexpr int MMA_WARPS = 2;         // warps 1 and 2 issue the MMAs
+    static constexpr int FIRST_EPI = 1 + MMA_WARPS;
+    // One store warp copies staged tiles out to C (and peers): a tile's copy-out
+    // is a few hundred store instructions against ~40 us of compute.  With 16
+    // epilogue warps that makes 20 warps, 96 registers a thread (a 21st warp
+    // would cut it to 80); with 8, 12 warps and 168.
+    static constexpr int STORE_WARPS = 1;
     static constexpr int CW = BN / EPI_SPLIT;  // columns per epilogue warp
-    static constexpr int THREADS = 64 + 32 * (EPI_WARPS + STORE_WARPS);
+    static constexpr int THREADS = 32 * (FIRST_EPI + EPI_WARPS + STORE_WARPS);
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -198,6 +207,9 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ TcParams p) {
     using Cfg = TcConfig<BN, EPI_SPLIT, OUT>;
     constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES, NBUF = Cfg::NBUF, CW = Cfg::CW;
+    // MMA-issuing threads: two in the chunked kernel (one per chunk of a pair),
+    // one in the FP32 kernels, whose single accumulator takes every MMA in order.
+    constexpr int ISSUERS = CHUNKED ? Cfg::MMA_WARPS : 1;
     static_assert(!(CHUNKED && REDO), "the redo pass runs in FP32 mode");
 
     extern __shared__ uint8_t smem_raw[];
@@ -222,18 +234,18 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty[s], ISSUERS);  // a commit from each MMA thread
         }
         for (int b = 0; b < NBUF; ++b) {
-            mbar_init(&tfull[b], 1);
+            mbar_init(&tfull[b], ISSUERS);
             mbar_init(&tempty[b], Cfg::EPI_WARPS);
         }
         for (int i = 0; i < kSchedDepth; ++i) {
             mbar_init(&ctrl->sched_full[i], 1);
-            mbar_init(&ctrl->sched_empty[i], 1 + Cfg::EPI_WARPS);  // the MMA thread and every epilogue warp
+            mbar_init(&ctrl->sched_empty[i], ISSUERS + Cfg::EPI_WARPS);  // the MMA threads, every epilogue warp
         }
         mbar_init(&ctrl->clc_bar, 1);
-        mbar_init(drain, 1);
+        mbar_init(drain, ISSUERS);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&ctrl->st_full[b], Cfg::EPI_WARPS);
             mbar_init(&ctrl->st_empty[b], Cfg::STORE_WARPS);
@@ -389,26 +401,37 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
                 if (pending & (1u << st)) mbar_wait_drain(&full[st], (pend_parity >> st) & 1u);
             if (clc_inflight) mbar_wait_drain(&ctrl->clc_bar, clc_phase);  // only after an abort
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+    } else if (warp < Cfg::FIRST_EPI) {
+        // ------------------------------------------------------------ MMA issuers
+        // Two issuing threads on different SM sub-partitions (warps 1 and 2): in a
+        // chunk pair, warp 1 issues chunk 2b and warp 2 chunk 2b+1, so the pair's
+        // MMAs are issued in parallel (each buffer's two K16 MMAs still come from
+        // one thread, which keeps them in order).  FP32 work accumulates into one
+        // buffer and is issued by warp 1 alone; warp 2 then only follows the
+        // barriers.  Every barrier the MMAs complete counts both threads' commits.
+        if (lane == 0 && warp <= ISSUERS) {
+            const bool second = warp == 2;
             constexpr uint32_t idesc = idesc_f16(!CHUNKED, B_MN, BM, BN);
             constexpr uint32_t idesc32 = idesc_f16(true, B_MN, BM, BN);
             const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
             uint32_t s = 0, ph = 0, b = 0, tph = 0;
-            // A whole tile's K loop with an FP32 accumulator in TMEM at d.
+            // A whole tile's K loop with an FP32 accumulator in TMEM at d (warp 1);
+            // warp 2 waits for and releases the same stages without MMAs.
             auto fp32_tile = [&](uint32_t d) -> bool {
                 for (int kb = 0; kb < nkb; ++kb) {
                     if (!mbar_wait(&full[s], ph, abort_flag, p.status, kStatusTimeoutMma)) return false;
                     tc_fence_after();
+                    if (!second) {
 #pragma unroll
-                    for (int ks = 0; ks < BK / 16; ++ks) {
-                        const int k16 = kb * (BK / 16) + ks;
-                        if (k16 >= nk16) break;
-                        const uint64_t ad = sdesc_sw128(sA0 + s * Cfg::A_BYTES + ks * 32, 16, 1024);
-                        const uint64_t bd = B_MN ? sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 2048, 64 * BK * 2, 1024)
-                                                 : sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 32, 16, 1024);
-                        umma_f16(d, ad, bd, idesc32, k16 > 0 ? 1u : 0u);
+                        for (int ks = 0; ks < BK / 16; ++ks) {
+                            const int k16 = kb * (BK / 16) + ks;
+                            if (k16 >= nk16) break;
+                            const uint64_t ad = sdesc_sw128(sA0 + s * Cfg::A_BYTES + ks * 32, 16, 1024);
+                            const uint64_t bd = B_MN
+                                                    ? sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 2048, 64 * BK * 2, 1024)
+                                                    : sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 32, 16, 1024);
+                            umma_f16(d, ad, bd, idesc32, k16 > 0 ? 1u : 0u);
+                        }
                     }
                     umma_commit(&empty[s]);
                     if (++s == STAGES) { s = 0; ph ^= 1u; }
@@ -440,6 +463,7 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
                         tc_fence_after();
 #pragma unroll
                         for (int cc = 0; cc < 2; ++cc) {
+                            if (cc != (second ? 1 : 0)) continue;  // this thread's chunk of the pair
                             const int c = kb * 2 + cc;
                             if (c >= nchunks) break;
                             const uint32_t d = tmem + (2 * b + cc) * Cfg::ACC_COLS;
@@ -472,9 +496,9 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
             umma_commit(drain);
             mbar_wait_drain(drain, 0);
         }
-    } else if (warp < 2 + Cfg::EPI_WARPS) {
+    } else if (warp < Cfg::FIRST_EPI + Cfg::EPI_WARPS) {
         // ------------------------------------------------------------ epilogue
-        const int e = warp - 2;          // epilogue warp index
+        const int e = warp - Cfg::FIRST_EPI;  // epilogue warp index
         const int q = warp & 3;          // TMEM lane quarter this warp may access
         const int colg = e >> 2;         // column slice
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
@@ -566,7 +590,7 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
         // kernel with the in-kernel redo, store warp 0 reads the OR of the 16
         // epilogue warps' flags, queues the tile for its FP32 redo if it is set,
         // and counts the tile as decided for the scheduler.
-        const int sw = warp - 2 - Cfg::EPI_WARPS;
+        const int sw = warp - Cfg::FIRST_EPI - Cfg::EPI_WARPS;
         void* dsts[1 + kMaxPeers] = {p.C};  // this GPU's C, then the peers' copies
         for (int i = 0; i < p.n_peers; ++i) dsts[1 + i] = p.peers[i];
         int decided = 0;

@@ -5,7 +5,8 @@
 //
 // Variants: 0 = the product's hand-off (wait, TMEM load, release, mixed adds);
 // 1 = the same without the adds; 2 = the MMA warp alone, issuing pairs
-// without waiting for releases (the tensor core's own issue rate).
+// without waiting for releases (the tensor core's own issue rate); 3 = as 0
+// with two MMA threads on different sub-partitions, one per chunk of a pair.
 #include <cuda_runtime.h>
 
 #include "launch.h"
@@ -37,12 +38,13 @@ __global__ void __launch_bounds__(64 + 128 * EPI_SPLIT, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < (BM + BN) * 64; i += blockDim.x)
         reinterpret_cast<__half*>(smem)[i] = __float2half(0.001f * (i & 63));
+    const int issuers = variant == 3 ? 2 : 1;  // variant 3: one MMA thread per chunk of a pair
     if (threadIdx.x == 0) {
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&tfull[b], 1);
+            mbar_init(&tfull[b], issuers);
             mbar_init(&tempty[b], EW);
         }
-        mbar_init(done, 1);
+        mbar_init(done, issuers);
         *abort_flag = 0;
         fence_mbarrier_init();
     }
@@ -59,9 +61,14 @@ __global__ void __launch_bounds__(64 + 128 * EPI_SPLIT, 1)
     // ev row per pair: [0] MMA warp woke  [1] after fence  [2] first MMA issued  [3] 4th MMA issued
     //                  [4] commit issued  [5] epilogue warp 0 woke  [6] epilogue warp 0 released
     //                  [7] last epilogue warp woke  [8] last epilogue warp released
-    if (warp == 1 && lane == 0) {
+    if ((warp == 1 || (warp == 0 && variant == 3)) && lane == 0) {
+        // variant 3: warp 1 issues chunk 0 of every pair, warp 0 chunk 1 (each buffer's two
+        // K16 MMAs from one thread, which keeps them in order); otherwise warp 1 issues both.
         constexpr uint32_t idesc = idesc_f16(false, false, BM, BN);
         const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+        const int k_lo = (variant == 3 && warp == 0) ? 1 : 0;
+        const int k_hi = (variant == 3 && warp == 1) ? 1 : 2;
+        const bool stamps = rec && warp == 1;
         uint32_t p = 0, ph = 0;
         for (int c2 = 0; c2 < npairs; ++c2, p ^= 1u) {
             if (variant != 2 && !mbar_wait(&tempty[p], ph ^ 1u, abort_flag, status, kStatusTimeoutProbe)) break;
@@ -69,18 +76,17 @@ __global__ void __launch_bounds__(64 + 128 * EPI_SPLIT, 1)
             t[0] = sm_clock();
             tc_fence_after();
             t[1] = sm_clock();
-#pragma unroll
-            for (int k = 0; k < 2; ++k)
+            for (int k = k_lo; k < k_hi; ++k)
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     umma_f16(tmem + (2 * p + k) * BN, sdesc_sw128(a0 + h * 32, 16, 1024),
                              sdesc_sw128(b0 + h * 32, 16, 1024), idesc, h);
-                    if (k == 0 && h == 0) t[2] = sm_clock();
+                    if (k == k_lo && h == 0) t[2] = sm_clock();
                 }
             t[3] = sm_clock();
             umma_commit(&tfull[p]);
             t[4] = sm_clock();
-            if (rec)
+            if (stamps)
 #pragma unroll
                 for (int i = 0; i < 5; ++i) ev[int64_t(c2) * 9 + i] = t[i];
             if (p == 1) ph ^= 1u;
@@ -113,7 +119,7 @@ __global__ void __launch_bounds__(64 + 128 * EPI_SPLIT, 1)
                 mbar_arrive(&tempty[p]);
                 if (mark) ev[int64_t(c2) * 9 + col + 1] = sm_clock();
             }
-            if (variant == 0) {
+            if (variant == 0 || variant == 3) {
                 add_chunk<CW>(acc, r0);
                 add_chunk<CW>(acc, r1);
             }

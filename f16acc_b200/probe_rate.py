@@ -57,9 +57,9 @@ def trace(dev: torch.device, npairs: int = 2048) -> int:
     npairs/10 .. 9*npairs/10 of CTA 0, all 148 CTAs running)."""
     lib = _lib.load()
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    names = ("pipeline", "pipeline_without_adds", "mma_warp_alone")
+    names = ("pipeline", "pipeline_without_adds", "mma_warp_alone", "pipeline_two_mma_threads")
     for epi in (4, 2):
-        for variant in (0, 1, 2):
+        for variant in (0, 1, 2, 3):
             ev = torch.zeros(npairs * 9, dtype=torch.int64, device=dev)
             out = torch.empty(sms * (64 + 128 * epi), device=dev)
             for _ in range(3):  # the last run's stamps are read

@@ -236,7 +236,8 @@ int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void 
  * fence, first MMA issued, fourth MMA issued, commit issued, epilogue warp 0
  * woke and released, last epilogue warp woke and released).  variant 0 = the
  * product's hand-off, 1 = without the FP32 adds, 2 = the MMA warp alone
- * (no waits; only its five stamps are written).  `out` holds
+ * (no waits; only its five stamps are written), 3 = as 0 with two MMA threads
+ * (one per chunk of a pair; the stamps are the first one's).  `out` holds
  * grid * (64 + 128*epi_split) floats. */
 int f16acc_probe_pair_trace(int variant, int epi_split, int npairs, int grid, void *events, void *out, int device,
                             void *stream);
