@@ -101,20 +101,23 @@ enum TcStore : int {
     kStoreEnd = 2,      // no tile: the epilogue is done
 };
 
-template <int BN_, int EPI_SPLIT_, int OUT_>
+template <int BN_, int EPI_SPLIT_, int OUT_, bool CHUNKED_>
 struct TcConfig {
     static constexpr int BM = 128;
     static constexpr int BN = BN_;
     static constexpr int BK = 64;  // one 128-byte swizzle row of f16 = two 32-long chunks
     static constexpr int EPI_SPLIT = EPI_SPLIT_;
     static constexpr int EPI_WARPS = 4 * EPI_SPLIT;
-    static constexpr int MMA_WARPS = 2;         // warps 1 and 2 issue the MMAs
+    // MMA-issuing warps: two in the chunked kernel (warps 1 and 2, one per chunk
+    // of a pair), one in the FP32 kernels, whose single accumulator takes every
+    // MMA in order.  Store warps copy staged tiles out to C (and peers): one in
+    // the chunked kernel (a tile's copy-out is a few hundred store instructions
+    // against ~40 us of compute), two in the FP32 kernels (a tile every ~25 us).
+    // Either way 16 epilogue warps make 20 warps, 96 registers a thread (a 21st
+    // warp would cut it to 80); 8 make 12 warps and 168.
+    static constexpr int MMA_WARPS = CHUNKED_ ? 2 : 1;
     static constexpr int FIRST_EPI = 1 + MMA_WARPS;
-    // One store warp copies staged tiles out to C (and peers): a tile's copy-out
-    // is a few hundred store instructions against ~40 us of compute.  With 16
-    // epilogue warps that makes 20 warps, 96 registers a thread (a 21st warp
-    // would cut it to 80); with 8, 12 warps and 168.
-    static constexpr int STORE_WARPS = 1;
+    static constexpr int STORE_WARPS = CHUNKED_ ? 1 : 2;
     static constexpr int CW = BN / EPI_SPLIT;  // columns per epilogue warp
     static constexpr int THREADS = 32 * (FIRST_EPI + EPI_WARPS + STORE_WARPS);
     static constexpr int A_BYTES = BM * BK * 2;
@@ -203,13 +206,11 @@ __device__ __forceinline__ void store_staged_strided(const uint8_t* staging, voi
 }
 
 template <int BN, int EPI_SPLIT, bool CHUNKED, bool B_MN, int OUT, bool REDO>
-__global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT>::THREADS, 1)
+__global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ TcParams p) {
-    using Cfg = TcConfig<BN, EPI_SPLIT, OUT>;
+    using Cfg = TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>;
     constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES, NBUF = Cfg::NBUF, CW = Cfg::CW;
-    // MMA-issuing threads: two in the chunked kernel (one per chunk of a pair),
-    // one in the FP32 kernels, whose single accumulator takes every MMA in order.
-    constexpr int ISSUERS = CHUNKED ? Cfg::MMA_WARPS : 1;
+    constexpr int ISSUERS = Cfg::MMA_WARPS;
     static_assert(!(CHUNKED && REDO), "the redo pass runs in FP32 mode");
 
     extern __shared__ uint8_t smem_raw[];

@@ -28,7 +28,7 @@ namespace {
 
 template <int BN, int EPI, bool CHUNKED, bool B_MN, int OUT, bool REDO>
 cudaError_t launch_one(const TcParams& p, int grid, cudaStream_t stream) {
-    using Cfg = TcConfig<BN, EPI, OUT>;
+    using Cfg = TcConfig<BN, EPI, OUT, CHUNKED>;
     auto kernel = tc_gemm_kernel<BN, EPI, CHUNKED, B_MN, OUT, REDO>;
     cudaError_t e = ensure_smem_attr(kernel, Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return e;
