@@ -5,7 +5,10 @@
  * each chunk is accumulated in FP16 on the tensor cores and added into an
  * FP32 accumulator.  Tiles whose FP16 chunk overflowed (any accumulator not
  * finite at the end) are flagged on the device and recomputed with FP32
- * accumulation by a second launch on the same stream, with no host sync.
+ * accumulation with no host sync: by default inside the same tcgen05 launch
+ * (the CTA that met the flag queues the tile and redoes it between its main
+ * tiles), otherwise by a second launch on the same stream (mma.sync path,
+ * f16acc_gemm_main / f16acc_gemm_redo, F16ACC_REDO_SEPARATE).
  *
  * Plain C: pointers, element strides, sizes; no CUDA or framework types.
  * `stream` is a cudaStream_t (NULL = legacy default stream) on `device`.
