@@ -115,9 +115,11 @@ Layout analyse(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t s
 }
 
 // tcgen05 tile configuration: output columns per tile and epilogue column
-// slices per TMEM lane quarter.  Process-wide; f16acc_set_tc_config changes
-// it (tuning and measurement), calls already issued keep theirs.
-std::atomic<int> g_tc_bn{128}, g_tc_epi{4};
+// slices per TMEM lane quarter (0 = by mode: 2 for the chunked kernel, whose
+// shorter release rounds with 8 epilogue warps measured faster, 4 for FP32
+// accumulation).  Process-wide; f16acc_set_tc_config changes it (tuning and
+// measurement), calls already issued keep theirs.
+std::atomic<int> g_tc_bn{128}, g_tc_epi{0};
 
 // Upper bound on the SMs a persistent launch may occupy (0 = all).  Leaving a
 // few SMs free lets kernels on other streams -- NCCL collectives overlapping a
@@ -127,7 +129,10 @@ int usable_sms(int sms) {
     const int lim = g_sm_limit.load(std::memory_order_relaxed);
     return lim > 0 && lim < sms ? lim : sms;
 }
-TcShape tc_shape() { return TcShape{g_tc_bn.load(std::memory_order_relaxed), g_tc_epi.load(std::memory_order_relaxed)}; }
+TcShape tc_shape(bool chunked) {
+    const int epi = g_tc_epi.load(std::memory_order_relaxed);
+    return TcShape{g_tc_bn.load(std::memory_order_relaxed), epi != 0 ? epi : (chunked ? 2 : 4)};
+}
 
 // Where flagged tiles of a chunked tcgen05 call are redone: 1 = inside the main
 // kernel, each CTA after its own main tiles; 0 = a second, dependent launch.
@@ -248,7 +253,7 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
     TcParams p;
     std::memset(&p, 0, sizeof(p));
     const bool b_mn = !L.b_tma_k;
-    const TcShape shape = tc_shape();
+    const TcShape shape = tc_shape(chunked != 0);
     if (v == F16ACC_VARIANT_TCGEN05) {
         const int bn = shape.bn;
         const bool maps_ok =
@@ -298,7 +303,7 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
             return F16ACC_ERR_CUDA;
         p.dyn_sched = 0;  // the separate redo pass walks the flags in static order
         if (chunked && (phases & kPhaseRedo) && !p.inline_redo &&
-            launch_tc(p, shape, false, b_mn, c_dtype, true, grid, stream) != cudaSuccess)
+            launch_tc(p, tc_shape(false), false, b_mn, c_dtype, true, grid, stream) != cudaSuccess)
             return F16ACC_ERR_CUDA;
         return F16ACC_OK;
     }
@@ -425,7 +430,7 @@ int f16acc_get_plan(const void* A, int64_t sAm, int64_t sAk, const void* B, int6
     if (v < 0) return variant == F16ACC_VARIANT_AUTO ? F16ACC_ERR_INVALID_ARGUMENT : F16ACC_ERR_UNSUPPORTED;
     out->variant = v;
     out->tile_m = v == F16ACC_VARIANT_SKINNY ? skinny_rows(M) : 128;
-    out->tile_n = v == F16ACC_VARIANT_TCGEN05 ? tc_shape().bn : (v == F16ACC_VARIANT_SKINNY ? SkinnyCfg::BN : MmaCfg::BN);
+    out->tile_n = v == F16ACC_VARIANT_TCGEN05 ? tc_shape(true).bn : (v == F16ACC_VARIANT_SKINNY ? SkinnyCfg::BN : MmaCfg::BN);
     out->tiles_m = cdiv(M, out->tile_m);
     out->tiles_n = cdiv(N, out->tile_n);
     return F16ACC_OK;
@@ -435,7 +440,7 @@ int f16acc_flag_bytes_per_tile(void) { return kFlagBytesPerTile; }
 
 int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void* out, int device, void* stream) {
     const bool known = (mode >= 0 && mode <= 15 && mode != 5) || (mode >= 20 && mode <= 28) ||
-                       (mode >= 30 && mode <= 36) || (mode >= 40 && mode <= 43) || mode == 45 || mode == 46;
+                       (mode >= 30 && mode <= 36) || (mode >= 40 && mode <= 43) || (mode >= 45 && mode <= 56);
     if (!known || chunks < 0 || grid <= 0 || out == nullptr) return F16ACC_ERR_INVALID_ARGUMENT;
     if (mode >= 2 && mode < 30 && epi_split != 2 && epi_split != 4) return F16ACC_ERR_INVALID_ARGUMENT;
     DeviceInfo* info = device_info(device);
@@ -450,7 +455,7 @@ int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void*
 
 int f16acc_probe_pair_trace(int variant, int epi_split, int npairs, int grid, void* events, void* out, int device,
                             void* stream) {
-    if (variant < 0 || variant > 3 || (epi_split != 2 && epi_split != 4) || npairs < 4 || grid <= 0 ||
+    if (variant < 0 || variant > 4 || (epi_split != 2 && epi_split != 4) || npairs < 4 || grid <= 0 ||
         events == nullptr || out == nullptr)
         return F16ACC_ERR_INVALID_ARGUMENT;
     DeviceInfo* info = device_info(device);
@@ -480,7 +485,7 @@ int f16acc_set_schedule(int mode) {
 }
 
 int f16acc_set_tc_config(int tile_n, int epi_split) {
-    if (!tc_shape_supported(TcShape{tile_n, epi_split})) return F16ACC_ERR_INVALID_ARGUMENT;
+    if (!tc_shape_supported(TcShape{tile_n, epi_split == 0 ? 4 : epi_split})) return F16ACC_ERR_INVALID_ARGUMENT;
     g_tc_bn.store(tile_n);
     g_tc_epi.store(epi_split);
     return F16ACC_OK;

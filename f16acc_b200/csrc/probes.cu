@@ -34,6 +34,34 @@ struct ProbeMode {
     static constexpr int NBUF = MODE == 20 ? 8 : 4;  // 20: ping-pong with 8 slots (no TMEM involved)
 };
 
+// Shared-memory flag signalling for probe modes 54 (release/acquire at CTA scope).
+__device__ __forceinline__ uint32_t ld_acquire_smem(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_smem(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_release_add_smem(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.cta.shared::cta.add.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+// Spin until *p >= target; bounded by kWaitLimitNs (clock read every 1024 polls).
+__device__ __forceinline__ bool spin_ge(const uint32_t* p, uint32_t target, int* status) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 1;; ++i) {
+        if (ld_acquire_smem(p) >= target) return true;
+        if ((i & 1023u) == 0u) {
+            const uint64_t now = globaltimer_ns();
+            if (t0 == 0) {
+                t0 = now;
+            } else if (now - t0 > kWaitLimitNs) {
+                atomicCAS(status, 0, kStatusTimeoutProbe);
+                return false;
+            }
+        }
+    }
+}
 template <int MODE, int EPI_SPLIT>
 __global__ void __launch_bounds__(64 + 128 * EPI_SPLIT, 1) chunk_rate_kernel(int chunks, float* out, int* status) {
     constexpr int BM = 128, BN = 128, NBUF = ProbeMode<MODE>::NBUF, CW = BN / EPI_SPLIT;
@@ -49,6 +77,8 @@ __global__ void __launch_bounds__(64 + 128 * EPI_SPLIT, 1) chunk_rate_kernel(int
     uint64_t* done = tempty + NBUF;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    uint32_t* flag_go = tmem_slot + 4;    // mode 54: issuer -> epilogue warps
+    uint32_t* flag_back = tmem_slot + 8;  // mode 54: epilogue warps -> issuer (a count)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     // operands: halves 1.0 / 0.0 alternating, so chunk sums stay small and finite
@@ -59,10 +89,14 @@ __global__ void __launch_bounds__(64 + 128 * EPI_SPLIT, 1) chunk_rate_kernel(int
         for (int b = 0; b < NBUF; ++b) {
             mbar_init(&tfull[b], 1);
             // mode 41: only the 8 warps that own a chunk (2 column slices x 4 quarters) release it
-            mbar_init(&tempty[b], (MODE == 41 || MODE == 46) ? 8 : (ProbeMode<MODE>::PER_THREAD ? 32 : 1) * 4 * EPI_SPLIT);
+            mbar_init(&tempty[b], (MODE == 41 || MODE == 46) ? 8
+                                  : (MODE == 51 || MODE == 52) ? 1
+                                                               : (ProbeMode<MODE>::PER_THREAD ? 32 : 1) * 4 * EPI_SPLIT);
         }
         mbar_init(done, 1);
         *abort_flag = 0;
+        *flag_go = 0;
+        *flag_back = 0;
         fence_mbarrier_init();
     }
     if (warp == 1) {
@@ -89,6 +123,86 @@ __global__ void __launch_bounds__(64 + 128 * EPI_SPLIT, 1) chunk_rate_kernel(int
                          idesc, h);
             umma_commit(done);
             if (!mbar_wait_drain(done, ph)) break;
+            ph ^= 1u;
+        }
+    } else if (warp == 1 && lane == 0 && MODE >= 47 && MODE <= 50) {
+        // latency detail, one thread per SM: 47 = 1 MMA + commit with a spinning wait;
+        // 48 = a commit alone (nothing in flight) with a suspending wait; 49 = the
+        // same with a spinning wait; 50 = 2 MMAs + commit with a spinning wait
+        constexpr int NM = MODE == 47 ? 1 : (MODE == 50 ? 2 : 0);
+        constexpr bool SPINW = MODE != 48;
+        constexpr uint32_t idesc = idesc_f16(false, false, BM, BN);
+        uint32_t ph = 0;
+        for (int c = 0; c < chunks; ++c) {
+#pragma unroll
+            for (int h = 0; h < NM; ++h)
+                umma_f16(tmem, sdesc_sw128(a0 + h * 32, 16, 1024), sdesc_sw128(b0 + h * 32, 16, 1024), idesc, h);
+            umma_commit(done);
+            const bool ok = SPINW ? mbar_wait_spin(done, ph, abort_flag, status, kStatusTimeoutProbe)
+                                  : mbar_wait(done, ph, abort_flag, status, kStatusTimeoutProbe);
+            if (!ok) break;
+            ph ^= 1u;
+        }
+    } else if ((MODE == 51 || MODE == 52) && (warp == 1 || warp == 2) && lane == 0) {
+        // mbarrier ping-pong between one thread of warp 1 and one of warp 2 (two
+        // sub-partitions), two hops per iteration: 51 suspending waits, 52 spinning
+        const bool ping = warp == 1;
+        uint32_t ph = 0;
+        for (int c = 0; c < chunks; ++c) {
+            if (ping) mbar_arrive(&tfull[0]);
+            uint64_t* w = ping ? &tempty[0] : &tfull[0];
+            const bool ok = MODE == 52 ? mbar_wait_spin(w, ph, abort_flag, status, kStatusTimeoutProbe)
+                                       : mbar_wait(w, ph, abort_flag, status, kStatusTimeoutProbe);
+            if (!ok) break;
+            if (!ping) mbar_arrive(&tempty[0]);
+            ph ^= 1u;
+        }
+    } else if (MODE >= 53 && MODE <= 56 && warp >= 1) {
+        // Release round trip between one issuing thread (warp 1) and the 16 epilogue
+        // warps, no MMAs: the issuer signals "go", every epilogue warp answers, the
+        // issuer waits for all 16 answers.  53: mbarriers both ways (the product's
+        // tfull/tempty); 54: shared-memory flags (a go word, an answer count);
+        // 55: named barriers both ways (bar.arrive / bar.sync, 17 warps);
+        // 56: an mbarrier out (as a commit would be) and a named barrier back.
+        // Every warp runs exactly `chunks` iterations with no early exit, so the
+        // named-barrier counts always match.
+        constexpr int NB = 32 * (1 + 4 * EPI_SPLIT);
+        const bool issuer = warp == 1;
+        uint32_t ph = 0;
+        for (int c = 0; c < chunks; ++c) {
+            if (issuer) {
+                if (MODE == 53 || MODE == 56) {
+                    if (lane == 0) mbar_arrive(&tfull[0]);
+                } else if (MODE == 54) {
+                    if (lane == 0) st_release_smem(flag_go, uint32_t(c + 1));
+                } else {
+                    named_bar_arrive(1, NB);
+                }
+                if (MODE == 53) {
+                    if (lane == 0) mbar_wait(&tempty[0], ph, abort_flag, status, kStatusTimeoutProbe);
+                } else if (MODE == 54) {
+                    if (lane == 0) spin_ge(flag_back, uint32_t(4 * EPI_SPLIT * (c + 1)), status);
+                } else {
+                    named_bar_sync(2, NB);
+                }
+                __syncwarp();
+            } else {
+                if (MODE == 53 || MODE == 56) {
+                    mbar_wait(&tfull[0], ph, abort_flag, status, kStatusTimeoutProbe);
+                } else if (MODE == 54) {
+                    if (lane == 0) spin_ge(flag_go, uint32_t(c + 1), status);
+                } else {
+                    named_bar_sync(1, NB);
+                }
+                __syncwarp();
+                if (MODE == 53) {
+                    if (lane == 0) mbar_arrive(&tempty[0]);
+                } else if (MODE == 54) {
+                    if (lane == 0) red_release_add_smem(flag_back, 1u);
+                } else {
+                    named_bar_arrive(2, NB);
+                }
+            }
             ph ^= 1u;
         }
     } else if (MODE == 46 && warp == 1 && lane == 0) {
@@ -663,6 +777,12 @@ cudaError_t launch_chunk_rate(int mode, int epi_split, int chunks, int grid, flo
             case 27: return launch_probe<27, 2>(chunks, grid, out, status, stream);
             case 28: return launch_probe<28, 2>(chunks, grid, out, status, stream);
             case 40: return launch_probe<40, 2>(chunks, grid, out, status, stream);
+            case 47: return launch_probe<47, 2>(chunks, grid, out, status, stream);
+            case 48: return launch_probe<48, 2>(chunks, grid, out, status, stream);
+            case 49: return launch_probe<49, 2>(chunks, grid, out, status, stream);
+            case 50: return launch_probe<50, 2>(chunks, grid, out, status, stream);
+            case 51: return launch_probe<51, 2>(chunks, grid, out, status, stream);
+            case 52: return launch_probe<52, 2>(chunks, grid, out, status, stream);
         }
     }
     if (epi_split == 4) {
@@ -676,6 +796,10 @@ cudaError_t launch_chunk_rate(int mode, int epi_split, int chunks, int grid, flo
             case 43: return launch_probe<43, 4>(chunks, grid, out, status, stream);
             case 45: return launch_probe<45, 4>(chunks, grid, out, status, stream);
             case 46: return launch_probe<46, 4>(chunks, grid, out, status, stream);
+            case 53: return launch_probe<53, 4>(chunks, grid, out, status, stream);
+            case 54: return launch_probe<54, 4>(chunks, grid, out, status, stream);
+            case 55: return launch_probe<55, 4>(chunks, grid, out, status, stream);
+            case 56: return launch_probe<56, 4>(chunks, grid, out, status, stream);
         }
     }
     return cudaErrorInvalidValue;

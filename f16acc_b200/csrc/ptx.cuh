@@ -117,6 +117,29 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, v
     }
 }
 
+// Named CTA barriers (IDs 1..15; 0 is __syncthreads).  `threads` counts every
+// thread of the participating warps; both are executed by whole warps.
+// bar.arrive marks arrival without waiting (release); bar.sync waits until
+// `threads` arrivals (acquire).  A bar.sync has no time limit, so callers
+// must guarantee that the arrivals it needs always come.
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(int id, int threads) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Wait bounded by `limit_ns` of %globaltimer only (no abort flag): true when
+// the phase completed in time.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer_ns() - t0 > limit_ns) return false;
+    }
+    return true;
+}
+
 // Wait used while shutting down after an abort: bounded by time only, so a
 // CTA can let its own in-flight copies and MMAs land before it exits.
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {

@@ -72,22 +72,57 @@ struct ChunkRing {
     }
 };
 
-// Chunk pairs: the MMA warp fills two chunk buffers (2p, 2p+1) per 64-wide
-// smem stage and signals them with one commit; the epilogue reads both and
-// releases them with one arrive.  Two pairs in flight (4 buffers).  Halving
-// the hand-offs per chunk is what pays: each hand-off costs a commit and two
-// barrier hops of latency, and only 4 chunk buffers fit in TMEM.
+// Chunk pairs: an MMA thread fills the two chunk buffers (2p, 2p+1) of pair p
+// from one 64-wide smem stage and signals them with one commit on tfull[p];
+// the epilogue reads both and releases the pair with one arrival on named
+// barrier kPairBarrier + p, on which the pair's MMA warp bar.syncs before
+// reusing it.  Two pairs in flight (4 buffers).  Handing chunks over in pairs
+// halves the hand-offs: each costs a commit and a barrier hop of latency, and
+// only 4 chunk buffers fit in TMEM.  The release is a named barrier rather
+// than an mbarrier because its round trip is about half as long (bar.arrive
+// wakes a bar.sync sooner than an mbarrier arrive wakes a try_wait).
+constexpr int kPairBarrier = 1;  // named barrier IDs 1 and 2, one per pair
+
 template <int CW>
 struct PairRing {
-    uint64_t* tfull;   // [2]
-    uint64_t* tempty;  // [2]
+    uint64_t* tfull;   // [2], one per pair
+    int bar_threads;   // threads of one MMA warp + the epilogue warps
     uint32_t col_base; // TMEM address of buffer 0 for this warp's lanes and column slice
     uint32_t stride;   // TMEM columns between chunk buffers
-    uint32_t p = 0, phase = 0;
+    uint32_t p = 0, phase = 0;  // pair of the next hand-off and its tfull phase parity
 
-    __device__ __forceinline__ void advance() {
+    // Wait for pair p's next hand-off (whole warp; false when the wait gave up).
+    __device__ __forceinline__ bool wait(volatile int* abort, int* status) {
+        const bool ok = mbar_wait(&tfull[p], phase, abort, status, kStatusTimeoutEpilogue);
+        return __all_sync(0xffffffffu, ok);
+    }
+    // Whole warp, after its TMEM loads of pair p have completed.
+    __device__ __forceinline__ void release() {
+        tc_fence_before();
+        __syncwarp();
+        named_bar_arrive(kPairBarrier + int(p), bar_threads);
         p ^= 1u;
         if (p == 0) phase ^= 1u;
+    }
+
+    // Whole warp, when leaving before the end (after raising the abort flag):
+    // arrive once for every hand-off that was issued and not yet released by
+    // this warp, so that an MMA warp in bar.sync on it wakes.  That is at most
+    // the next hand-off of each pair (a pair's MMA warp issues into it again
+    // only after every epilogue warp released it), and it was issued exactly
+    // when its tfull completes, which the MMAs do within microseconds (waited
+    // for up to 20 ms).  Arriving only for issued hand-offs never puts a second
+    // arrival of this warp into a round.
+    __device__ __forceinline__ void release_issued_on_exit(int lane) {
+        uint32_t pp = p, ph = phase;
+        for (int k = 0; k < 2; ++k) {
+            bool issued = false;
+            if (lane == 0) issued = mbar_wait_for(&tfull[pp], ph, 20000000ull);
+            issued = __shfl_sync(0xffffffffu, issued, 0);
+            if (issued) named_bar_arrive(kPairBarrier + int(pp), bar_threads);
+            pp ^= 1u;
+            if (pp == 0) ph ^= 1u;
+        }
     }
 };
 
@@ -95,11 +130,10 @@ struct PairRing {
 // a tile holds one chunk when nchunks is odd.  Returns false when a wait gave
 // up (no TMEM load is left in flight then).
 template <int CW>
-__device__ __forceinline__ bool consume_chunk_pairs(float (&acc)[CW], int nchunks, PairRing<CW>& ring, int lane,
+__device__ __forceinline__ bool consume_chunk_pairs(float (&acc)[CW], int nchunks, PairRing<CW>& ring,
                                                     volatile int* abort, int* status) {
     for (int c = 0; c < nchunks; c += 2) {
-        const bool ok = mbar_wait(&ring.tfull[ring.p], ring.phase, abort, status, kStatusTimeoutEpilogue);
-        if (!__all_sync(0xffffffffu, ok)) return false;
+        if (!ring.wait(abort, status)) return false;
         tc_fence_after();
         const bool two = c + 1 < nchunks;
         const uint32_t a0 = ring.col_base + (2 * ring.p) * ring.stride;
@@ -109,10 +143,7 @@ __device__ __forceinline__ bool consume_chunk_pairs(float (&acc)[CW], int nchunk
         tmem_wait_ld();
         reg_fence(r0);
         if (two) reg_fence(r1);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ring.tempty[ring.p]);
-        ring.advance();
+        ring.release();
         add_chunk<CW>(acc, r0);
         if (two) add_chunk<CW>(acc, r1);
     }
@@ -122,10 +153,9 @@ __device__ __forceinline__ bool consume_chunk_pairs(float (&acc)[CW], int nchunk
 // One FP32 accumulator (a whole redo tile) handed over through the pair ring:
 // it sits in the pair's first chunk buffer.  Returns false when the wait gave up.
 template <int CW>
-__device__ __forceinline__ bool consume_fp32_pair(float (&acc)[CW], PairRing<CW>& ring, int lane,
-                                                  volatile int* abort, int* status) {
-    const bool ok = mbar_wait(&ring.tfull[ring.p], ring.phase, abort, status, kStatusTimeoutEpilogue);
-    if (!__all_sync(0xffffffffu, ok)) return false;
+__device__ __forceinline__ bool consume_fp32_pair(float (&acc)[CW], PairRing<CW>& ring, volatile int* abort,
+                                                  int* status) {
+    if (!ring.wait(abort, status)) return false;
     tc_fence_after();
     const uint32_t a0 = ring.col_base + (2 * ring.p) * ring.stride;
 #pragma unroll
@@ -137,10 +167,7 @@ __device__ __forceinline__ bool consume_fp32_pair(float (&acc)[CW], PairRing<CW>
 #pragma unroll
         for (int k = 0; k < 32; ++k) acc[j * 32 + k] = __uint_as_float(r[k]);
     }
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&ring.tempty[ring.p]);
-    ring.advance();
+    ring.release();
     return true;
 }
 

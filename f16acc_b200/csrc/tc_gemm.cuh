@@ -235,10 +235,10 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], ISSUERS);  // a commit from each MMA thread
+            mbar_init(&empty[s], 1);  // the commit of the MMA thread that read the stage
         }
         for (int b = 0; b < NBUF; ++b) {
-            mbar_init(&tfull[b], ISSUERS);
+            mbar_init(&tfull[b], 1);  // the commit of the MMA thread that filled it (chunked: pair b)
             mbar_init(&tempty[b], Cfg::EPI_WARPS);
         }
         for (int i = 0; i < kSchedDepth; ++i) {
@@ -404,25 +404,57 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
         }
     } else if (warp < Cfg::FIRST_EPI) {
         // ------------------------------------------------------------ MMA issuers
-        // Two issuing threads on different SM sub-partitions (warps 1 and 2): in a
-        // chunk pair, warp 1 issues chunk 2b and warp 2 chunk 2b+1, so the pair's
-        // MMAs are issued in parallel (each buffer's two K16 MMAs still come from
-        // one thread, which keeps them in order).  FP32 work accumulates into one
-        // buffer and is issued by warp 1 alone; warp 2 then only follows the
-        // barriers.  Every barrier the MMAs complete counts both threads' commits.
-        if (lane == 0 && warp <= ISSUERS) {
-            const bool second = warp == 2;
+        // Chunked kernel: two MMA warps on different SM sub-partitions take the
+        // hand-offs (chunk pairs, FP32 redo tiles) alternately: hand-off n goes
+        // through pair b = n & 1 and is issued by warp 1 + b, so one warp issues
+        // pair n while the other issues pair n+1.  Pair b is reclaimed with
+        // bar.sync on named barrier kPairBarrier + b, whose rounds are that one
+        // warp plus every epilogue warp.  FP32 kernel: one thread, mbarriers only.
+        // Hang freedom of the bar.sync: (1) each named barrier has one waiter,
+        // warp 1 + b, which issues into pair b again only after the round
+        // completes; (2) it checks the abort flag (warp-uniformly) before issuing
+        // and before and after every bar.sync; (3) an epilogue warp that leaves
+        // early raises the flag and then arrives once for each hand-off issued
+        // and not yet released by it (at most one per pair, found issued by its
+        // tfull completing), so the round a waiter is in always fills, and never
+        // overfills.
+        constexpr int NB = 32 * (1 + Cfg::EPI_WARPS);  // release-barrier threads
+        if (warp <= ISSUERS && (CHUNKED || lane == 0)) {
+            const uint32_t mine = uint32_t(warp - 1);  // chunked: the pair this warp issues into
+            const bool issue = lane == 0;
             constexpr uint32_t idesc = idesc_f16(!CHUNKED, B_MN, BM, BN);
             constexpr uint32_t idesc32 = idesc_f16(true, B_MN, BM, BN);
             const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
             uint32_t s = 0, ph = 0, b = 0, tph = 0;
-            // A whole tile's K loop with an FP32 accumulator in TMEM at d (warp 1);
-            // warp 2 waits for and releases the same stages without MMAs.
+            bool pending = false;  // chunked: a hand-off issued into `mine` and not yet reclaimed
+            // A bounded mbarrier wait, uniform across the warp in the chunked kernel.
+            auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+                const bool ok = mbar_wait(bar, parity, abort_flag, p.status, kStatusTimeoutMma);
+                if constexpr (CHUNKED) return __all_sync(0xffffffffu, ok);
+                return ok;
+            };
+            auto aborted = [&]() -> bool { return __any_sync(0xffffffffu, *abort_flag != 0); };
+            // Before issuing into pair `mine` (chunked): wait until every epilogue
+            // warp has loaded the hand-off issued into it before.  False when the
+            // kernel is aborting.
+            auto reclaim = [&]() -> bool {
+                if (aborted()) return false;
+                if (pending) {
+                    named_bar_sync(kPairBarrier + int(mine), NB);
+                    pending = false;
+                    if (aborted()) return false;
+                }
+                return true;
+            };
+            auto next_stage = [&]() {
+                if (++s == STAGES) { s = 0; ph ^= 1u; }
+            };
+            // A whole tile's K loop with an FP32 accumulator in TMEM at d.
             auto fp32_tile = [&](uint32_t d) -> bool {
                 for (int kb = 0; kb < nkb; ++kb) {
-                    if (!mbar_wait(&full[s], ph, abort_flag, p.status, kStatusTimeoutMma)) return false;
+                    if (!wait(&full[s], ph)) return false;
                     tc_fence_after();
-                    if (!second) {
+                    if (issue) {
 #pragma unroll
                         for (int ks = 0; ks < BK / 16; ++ks) {
                             const int k16 = kb * (BK / 16) + ks;
@@ -433,56 +465,73 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
                                                     : sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 32, 16, 1024);
                             umma_f16(d, ad, bd, idesc32, k16 > 0 ? 1u : 0u);
                         }
+                        umma_commit(&empty[s]);
                     }
-                    umma_commit(&empty[s]);
-                    if (++s == STAGES) { s = 0; ph ^= 1u; }
+                    if constexpr (CHUNKED) __syncwarp();
+                    next_stage();
                 }
                 return true;
             };
+            bool normal_end = false;
             for (uint32_t qi = 0, qph = 0;;) {
-                if (!mbar_wait(&ctrl->sched_full[qi], qph, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
+                if (!wait(&ctrl->sched_full[qi], qph)) goto mma_done;
                 const int kind = ctrl->sched[qi].z;
-                mbar_arrive(&ctrl->sched_empty[qi]);
+                if constexpr (CHUNKED) __syncwarp();
+                if (issue) mbar_arrive(&ctrl->sched_empty[qi]);
                 if (++qi == kSchedDepth) { qi = 0; qph ^= 1u; }
-                if (kind == kWorkEnd) break;
+                if (kind == kWorkEnd) {
+                    normal_end = true;
+                    break;
+                }
                 if (CHUNKED && kind == kWorkRedo) {
                     // A flagged tile in FP32 mode: the K16 MMA sequence of the FP32 kernel
                     // (so bit-identical results), accumulated in chunk buffer 2b and handed
-                    // over through pair b like one chunk pair.
-                    if (!mbar_wait(&tempty[b], tph ^ 1u, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
-                    tc_fence_after();
-                    if (!fp32_tile(tmem + (2 * b) * Cfg::ACC_COLS)) goto mma_done;
-                    umma_commit(&tfull[b]);
+                    // over through pair b like one chunk pair.  The other MMA warp steps
+                    // over its stages.
+                    if (b == mine) {
+                        if (!reclaim()) goto mma_done;
+                        tc_fence_after();
+                        if (!fp32_tile(tmem + (2 * b) * Cfg::ACC_COLS)) goto mma_done;
+                        if (issue) umma_commit(&tfull[b]);
+                        __syncwarp();
+                        pending = true;
+                    } else {
+                        for (int kb = 0; kb < nkb; ++kb) next_stage();
+                    }
                     b ^= 1u;
-                    if (b == 0) tph ^= 1u;
                 } else if constexpr (CHUNKED) {
                     // One hand-off per 64-wide stage: its two 32-long chunks go to the
-                    // chunk buffers 2b and 2b+1 of pair b (two pairs in flight), one commit.
+                    // chunk buffers 2b and 2b+1 of pair b, issued by warp 1 + b.
                     for (int kb = 0; kb < nkb; ++kb) {
-                        if (!mbar_wait(&full[s], ph, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
-                        if (!mbar_wait(&tempty[b], tph ^ 1u, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
-                        tc_fence_after();
+                        if (b == mine) {
+                            if (!wait(&full[s], ph)) goto mma_done;
+                            if (!reclaim()) goto mma_done;
+                            tc_fence_after();
+                            if (issue) {
 #pragma unroll
-                        for (int cc = 0; cc < 2; ++cc) {
-                            if (cc != (second ? 1 : 0)) continue;  // this thread's chunk of the pair
-                            const int c = kb * 2 + cc;
-                            if (c >= nchunks) break;
-                            const uint32_t d = tmem + (2 * b + cc) * Cfg::ACC_COLS;
+                                for (int cc = 0; cc < 2; ++cc) {
+                                    const int c = kb * 2 + cc;
+                                    if (c >= nchunks) break;
+                                    const uint32_t d = tmem + (2 * b + cc) * Cfg::ACC_COLS;
 #pragma unroll
-                            for (int h = 0; h < 2; ++h) {
-                                const int ks = cc * 2 + h;
-                                if (h == 1 && c * 32 + 16 >= p.K) break;  // K16 step past the end adds nothing
-                                const uint64_t ad = sdesc_sw128(sA0 + s * Cfg::A_BYTES + ks * 32, 16, 1024);
-                                const uint64_t bd = B_MN ? sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 2048, 64 * BK * 2, 1024)
-                                                         : sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 32, 16, 1024);
-                                umma_f16(d, ad, bd, idesc, h);
+                                    for (int h = 0; h < 2; ++h) {
+                                        const int ks = cc * 2 + h;
+                                        if (h == 1 && c * 32 + 16 >= p.K) break;  // K16 step past the end adds nothing
+                                        const uint64_t ad = sdesc_sw128(sA0 + s * Cfg::A_BYTES + ks * 32, 16, 1024);
+                                        const uint64_t bd =
+                                            B_MN ? sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 2048, 64 * BK * 2, 1024)
+                                                 : sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 32, 16, 1024);
+                                        umma_f16(d, ad, bd, idesc, h);
+                                    }
+                                }
+                                umma_commit(&tfull[b]);
+                                umma_commit(&empty[s]);
                             }
+                            __syncwarp();
+                            pending = true;
                         }
-                        umma_commit(&tfull[b]);
-                        umma_commit(&empty[s]);
                         b ^= 1u;
-                        if (b == 0) tph ^= 1u;
-                        if (++s == STAGES) { s = 0; ph ^= 1u; }
+                        next_stage();
                     }
                 } else {
                     if (!mbar_wait(&tempty[b], tph ^ 1u, abort_flag, p.status, kStatusTimeoutMma)) goto mma_done;
@@ -493,9 +542,18 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
                 }
             }
         mma_done:
+            if constexpr (CHUNKED) {
+                // Reclaim the last hand-off in `mine` so every round of its barrier is
+                // complete when the kernel ends (skipped when aborting: nothing waits
+                // on this warp then).
+                if (normal_end && pending && !aborted()) named_bar_sync(kPairBarrier + int(mine), NB);
+            }
             // All MMAs issued by this thread complete before TMEM is freed.
-            umma_commit(drain);
-            mbar_wait_drain(drain, 0);
+            if (issue) {
+                umma_commit(drain);
+                mbar_wait_drain(drain, 0);
+            }
+            if constexpr (CHUNKED) __syncwarp();
         }
     } else if (warp < Cfg::FIRST_EPI + Cfg::EPI_WARPS) {
         // ------------------------------------------------------------ epilogue
@@ -504,7 +562,8 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
         const int colg = e >> 2;         // column slice
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
         ChunkRing<NBUF> ring{tfull, tempty, tmem + lane_base + colg * CW, Cfg::ACC_COLS};    // FP32 mode
-        PairRing<CW> pairs{tfull, tempty, tmem + lane_base + colg * CW, Cfg::ACC_COLS};     // chunked mode
+        constexpr int NB = 32 * (1 + Cfg::EPI_WARPS);  // pair-barrier threads: one MMA warp + the epilogue
+        PairRing<CW> pairs{tfull, NB, tmem + lane_base + colg * CW, Cfg::ACC_COLS};     // chunked mode
         // Finished tiles go to the store warps through the staging tiles, in order:
         // tile k in staging k % SBUF.  take_staging waits until the store warps have
         // copied out that buffer's previous tile; hand_over passes the staged tile
@@ -544,7 +603,7 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
                 if (main_item) {
 #pragma unroll
                     for (int j = 0; j < CW; ++j) acc[j] = 0.0f;
-                    if (!consume_chunk_pairs<CW>(acc, nchunks, pairs, lane, abort_flag, p.status)) break;
+                    if (!consume_chunk_pairs<CW>(acc, nchunks, pairs, abort_flag, p.status)) break;
                     float z = 0.0f;
 #pragma unroll
                     for (int j = 0; j < CW; ++j) z = nonfinite_probe(z, acc[j]);
@@ -557,7 +616,7 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
                             slot[e] = bad ? 1 : 0;
                     }
                 } else {
-                    if (!consume_fp32_pair<CW>(acc, pairs, lane, abort_flag, p.status)) break;
+                    if (!consume_fp32_pair<CW>(acc, pairs, abort_flag, p.status)) break;
                 }
             } else {
                 if (!ring.wait_full(abort_flag, p.status)) break;
@@ -579,6 +638,15 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
             const bool decide = inline_redo && main_item;
             if (decide && bad && lane == 0) atomicOr(&ctrl->tile_bad[b], 1);
             hand_over(tm, tn, decide ? kStoreDecide : kStoreTile);
+        }
+        if (CHUNKED && !finished) {
+            // Leaving early (a wait gave up): raise the abort flag, then release the
+            // pairs issued to this warp, so that an MMA warp waiting in bar.sync on
+            // one wakes, sees the flag and stops.
+            *abort_flag = 1;
+            __threadfence_block();
+            __syncwarp();
+            pairs.release_issued_on_exit(lane);
         }
         if (finished && take_staging()) hand_over(0, 0, kStoreEnd);
     } else {

@@ -6,7 +6,10 @@
 // Variants: 0 = the product's hand-off (wait, TMEM load, release, mixed adds);
 // 1 = the same without the adds; 2 = the MMA warp alone, issuing pairs
 // without waiting for releases (the tensor core's own issue rate); 3 = as 0
-// with two MMA threads on different sub-partitions, one per chunk of a pair.
+// with two MMA threads on different sub-partitions, one per chunk of a pair;
+// 4 = as 3, and the epilogue warps of the two issuing sub-partitions start
+// their adds only once their sub-partition's MMA thread has issued into the
+// buffers they just released (the other two sub-partitions add at once).
 #include <cuda_runtime.h>
 
 #include "launch.h"
@@ -33,18 +36,21 @@ __global__ void __launch_bounds__(64 + 128 * EPI_SPLIT, 1)
     uint64_t* tfull = reinterpret_cast<uint64_t*>(sB + BN * 64 * 2);
     uint64_t* tempty = tfull + 2;
     uint64_t* done = tempty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* issued = done + 1;  // [sub-partition 0..1][buffer pair 0..1], variant 4
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(issued + 4);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < (BM + BN) * 64; i += blockDim.x)
         reinterpret_cast<__half*>(smem)[i] = __float2half(0.001f * (i & 63));
-    const int issuers = variant == 3 ? 2 : 1;  // variant 3: one MMA thread per chunk of a pair
+    const bool two = variant == 3 || variant == 4;  // one MMA thread per chunk of a pair
+    const int issuers = two ? 2 : 1;
     if (threadIdx.x == 0) {
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], issuers);
             mbar_init(&tempty[b], EW);
         }
         mbar_init(done, issuers);
+        for (int i = 0; i < 4; ++i) mbar_init(&issued[i], 1);
         *abort_flag = 0;
         fence_mbarrier_init();
     }
@@ -61,13 +67,13 @@ __global__ void __launch_bounds__(64 + 128 * EPI_SPLIT, 1)
     // ev row per pair: [0] MMA warp woke  [1] after fence  [2] first MMA issued  [3] 4th MMA issued
     //                  [4] commit issued  [5] epilogue warp 0 woke  [6] epilogue warp 0 released
     //                  [7] last epilogue warp woke  [8] last epilogue warp released
-    if ((warp == 1 || (warp == 0 && variant == 3)) && lane == 0) {
+    if ((warp == 1 || (warp == 0 && two)) && lane == 0) {
         // variant 3: warp 1 issues chunk 0 of every pair, warp 0 chunk 1 (each buffer's two
         // K16 MMAs from one thread, which keeps them in order); otherwise warp 1 issues both.
         constexpr uint32_t idesc = idesc_f16(false, false, BM, BN);
         const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
-        const int k_lo = (variant == 3 && warp == 0) ? 1 : 0;
-        const int k_hi = (variant == 3 && warp == 1) ? 1 : 2;
+        const int k_lo = (two && warp == 0) ? 1 : 0;
+        const int k_hi = (two && warp == 1) ? 1 : 2;
         const bool stamps = rec && warp == 1;
         uint32_t p = 0, ph = 0;
         for (int c2 = 0; c2 < npairs; ++c2, p ^= 1u) {
@@ -84,6 +90,7 @@ __global__ void __launch_bounds__(64 + 128 * EPI_SPLIT, 1)
                     if (k == k_lo && h == 0) t[2] = sm_clock();
                 }
             t[3] = sm_clock();
+            if (variant == 4) mbar_arrive(&issued[warp * 2 + p]);
             umma_commit(&tfull[p]);
             t[4] = sm_clock();
             if (stamps)
@@ -119,7 +126,14 @@ __global__ void __launch_bounds__(64 + 128 * EPI_SPLIT, 1)
                 mbar_arrive(&tempty[p]);
                 if (mark) ev[int64_t(c2) * 9 + col + 1] = sm_clock();
             }
-            if (variant == 0 || variant == 3) {
+            // variant 4: the issuing sub-partitions wait for the issue of pair
+            // c2 + 2 into the buffers just released (issue number c2/2 + 1 there)
+            if (variant == 4 && q < 2 && c2 + 2 < npairs) {
+                const bool ok2 = mbar_wait(&issued[q * 2 + p], uint32_t((c2 >> 1) + 1) & 1u, abort_flag, status,
+                                           kStatusTimeoutProbe);
+                if (!__all_sync(0xffffffffu, ok2)) break;
+            }
+            if (variant == 0 || variant == 3 || variant == 4) {
                 add_chunk<CW>(acc, r0);
                 add_chunk<CW>(acc, r1);
             }

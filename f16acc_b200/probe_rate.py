@@ -57,9 +57,10 @@ def trace(dev: torch.device, npairs: int = 2048) -> int:
     npairs/10 .. 9*npairs/10 of CTA 0, all 148 CTAs running)."""
     lib = _lib.load()
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    names = ("pipeline", "pipeline_without_adds", "mma_warp_alone", "pipeline_two_mma_threads")
+    names = ("pipeline", "pipeline_without_adds", "mma_warp_alone", "pipeline_two_mma_threads",
+             "pipeline_two_mma_threads_issuer_first")
     for epi in (4, 2):
-        for variant in (0, 1, 2, 3):
+        for variant in (0, 1, 2, 3, 4):
             ev = torch.zeros(npairs * 9, dtype=torch.int64, device=dev)
             out = torch.empty(sms * (64 + 128 * epi), device=dev)
             for _ in range(3):  # the last run's stamps are read
@@ -87,15 +88,37 @@ def trace(dev: torch.device, npairs: int = 2048) -> int:
     return 0
 
 
+def latency(dev: torch.device, chunks: int, reps: int) -> int:
+    """One thread per SM: a dependent MMA group + commit + mbarrier wait per
+    iteration (suspending or spinning waits), and a two-thread mbarrier
+    ping-pong; cycles per iteration at the sampled SM clock."""
+    lat = [("latency_2mma_n128", 8), ("latency_1mma_n128", 9), ("latency_2mma_n64", 10), ("latency_8mma_n128", 11),
+           ("latency_1mma_n128_spin", 47), ("latency_commit_only", 48), ("latency_commit_only_spin", 49),
+           ("latency_2mma_n128_spin", 50), ("latency_pingpong_2hops", 51), ("latency_pingpong_2hops_spin", 52)]
+    lat += [("roundtrip_16warps_mbarriers", 53), ("roundtrip_16warps_smem_flags", 54),
+            ("roundtrip_16warps_named_barriers", 55), ("roundtrip_16warps_mbarrier_out_named_back", 56)]
+    iters = max(256, chunks // 16)
+    for name, mode in lat:
+        sms, ms, _, clk = run(mode, 4 if mode >= 53 else 2, iters, reps, dev)
+        ns = ms * 1e6 / iters
+        mhz = clk.get("sm_mhz") or 0
+        print(json.dumps({"probe": name, "iters": iters, "ns_per_group": ns,
+                          "cycles_per_group": ns * mhz / 1e3 if mhz else None, "clocks": clk}), flush=True)
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--chunks", type=int, default=4096)
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--trace", action="store_true", help="only the timed pair hand-off (per-step SM cycles)")
+    ap.add_argument("--latency", action="store_true", help="only the latency probes")
     a = ap.parse_args(argv)
     dev = torch.device("cuda:0")
     if a.trace:
         return trace(dev)
+    if a.latency:
+        return latency(dev, a.chunks, a.reps)
     probes = [("mma_f16acc", 0, 2), ("mma_f32acc", 1, 2), ("chunk_pipeline_8warp", 2, 2),
               ("chunk_pipeline_16warp", 2, 4), ("pipeline_no_adds_8warp", 3, 2), ("pipeline_no_adds_16warp", 3, 4),
               ("handoff_only_8warp", 4, 2), ("tmem_ld_only_8warp", 6, 2), ("tmem_ld_only_16warp", 6, 4),
@@ -148,15 +171,7 @@ def main(argv=None) -> int:
         peak = sms * 8192 * mhz * 1e6 / 1e12 if mhz else None
         print(json.dumps({"probe": name, "iters": iters, "ms": ms, "tflops": tflops, "clocks": clk,
                           "frac_of_clock_peak": tflops / peak if peak else None}), flush=True)
-    # latency: one thread, a dependent MMA group + commit + mbarrier wait per iteration
-    lat = [("latency_2mma_n128", 8), ("latency_1mma_n128", 9), ("latency_2mma_n64", 10), ("latency_8mma_n128", 11)]
-    iters = max(256, a.chunks // 16)
-    for name, mode in lat:
-        sms, ms, _, clk = run(mode, 2, iters, a.reps, dev)
-        ns = ms * 1e6 / iters
-        mhz = clk.get("sm_mhz") or 0
-        print(json.dumps({"probe": name, "iters": iters, "ns_per_group": ns,
-                          "cycles_per_group": ns * mhz / 1e3 if mhz else None, "clocks": clk}), flush=True)
+    latency(dev, a.chunks, a.reps)
     st = _lib.load().f16acc_device_status(dev.index or 0, 1)
     if st != 0:
         print(json.dumps({"device_status": st}))

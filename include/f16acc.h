@@ -165,8 +165,8 @@ int f16acc_flag_bytes_per_tile(void);
 
 /* tcgen05 tile configuration for later calls, process-wide: output columns
  * per tile (128) and epilogue column slices per TMEM lane quarter (2 or 4,
- * i.e. 8 or 16 epilogue warps).  A tuning knob; do not change it between an
- * f16acc_gemm_main and its f16acc_gemm_redo. */
+ * i.e. 8 or 16 epilogue warps; 0 = the default, 2 for chunked accumulation
+ * and 4 for FP32 accumulation).  A tuning knob; results do not depend on it. */
 int f16acc_set_tc_config(int tile_n, int epi_split);
 
 /* Cap the SMs a GEMM launch occupies, process-wide, for later calls (0 = all
@@ -240,7 +240,9 @@ int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void 
  * woke and released, last epilogue warp woke and released).  variant 0 = the
  * product's hand-off, 1 = without the FP32 adds, 2 = the MMA warp alone
  * (no waits; only its five stamps are written), 3 = as 0 with two MMA threads
- * (one per chunk of a pair; the stamps are the first one's).  `out` holds
+ * (one per chunk of a pair; the stamps are the first one's), 4 = as 3 with
+ * the epilogue warps of the two issuing sub-partitions starting their adds
+ * only after their MMA thread has issued the next pair.  `out` holds
  * grid * (64 + 128*epi_split) floats. */
 int f16acc_probe_pair_trace(int variant, int epi_split, int npairs, int grid, void *events, void *out, int device,
                             void *stream);
