@@ -65,17 +65,18 @@ EncodeTiledFn encode_fn() {
     return g_encode;
 }
 
-// 2-D FP16 tensor map: inner dimension d0 (contiguous), outer d1 with byte
-// stride stride1, box {b0, b1}, 128-byte swizzle, zero fill out of bounds.
+// 2-D tensor map (FP16 unless `dtype` says otherwise): inner dimension d0
+// (contiguous), outer d1 with byte stride stride1, box {b0, b1}, 128-byte
+// swizzle, zero fill out of bounds.
 bool make_map(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t stride1_bytes, uint32_t b0,
-              uint32_t b1) {
+              uint32_t b1, CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_FLOAT16) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return false;
     const cuuint64_t dims[2] = {d0, d1};
     const cuuint64_t strides[1] = {stride1_bytes};
     const cuuint32_t box[2] = {b0, b1};
     const cuuint32_t estr[2] = {1, 1};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+    return enc(m, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -285,6 +286,17 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
         for (int i = 0; i < n_peers; ++i) p.peers[i] = peers[i];
         p.bias = static_cast<const __half*>(bias);
         p.sbias = sbias;
+        // Finished tiles leave through TMA stores when C allows (row-major, 16-byte
+        // aligned rows) and nothing else has to be written with them.
+        if (p.c_vec && n_peers == 0 && bias == nullptr) {
+            const CUtensorMapDataType ct = c_dtype == F16ACC_OUT_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                           : c_dtype == F16ACC_OUT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+            p.tma_store = make_map(&p.tmC, C, uint64_t(N), uint64_t(M), uint64_t(sCm) * esize, 128 / uint32_t(esize),
+                                   128, ct)
+                              ? 1
+                              : 0;
+        }
         const int64_t tiles = int64_t(p.tiles_m) * p.tiles_n;
         if (tiles >= (int64_t(1) << 31)) return F16ACC_ERR_INVALID_ARGUMENT;
         const int sms = usable_sms(info->sms);

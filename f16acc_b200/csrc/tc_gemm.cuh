@@ -40,6 +40,11 @@ namespace f16acc {
 struct TcParams {
     CUtensorMap tmA;  // A [M, K], K contiguous: dims {K, M}, box {64, 128}
     CUtensorMap tmB;  // B K-contiguous: dims {K, N}, box {64, BN};  N-contiguous: dims {N, K}, box {64, 64}
+    CUtensorMap tmC;  // C row-major, when tma_store: dims {N, M}, box {128 bytes of columns, 128 rows}
+    // Finished tiles leave through TMA stores (C row-major and 16-byte aligned,
+    // no bias, no peers): staged in 128-byte-swizzled boxes, one bulk tensor
+    // store per box.  Otherwise the store warps copy them out with plain stores.
+    int tma_store;
     void* C;
     int64_t sCm, sCn;
     int M, N, K;
@@ -154,6 +159,23 @@ __device__ __forceinline__ void stage_row(uint8_t* staging, int row_in_tile, int
     uint8_t* dst = staging + row_in_tile * PITCH + col_in_tile * int(sizeof(typename Tr::T));
 #pragma unroll
     for (int j = 0; j < CW; j += Tr::kVec) *reinterpret_cast<uint4*>(dst + j * int(sizeof(typename Tr::T))) = pack16<OUT>(&acc[j]);
+}
+
+// Stage one thread's row segment for the TMA store: the tile is kept as
+// BN*sizeof(T)/128 boxes of BM rows x 128 bytes, each with the 128-byte
+// swizzle of the C tensor map (16-byte piece w of row r at position w ^ (r % 8)
+// of the row), which also spreads a warp's rows over all banks.
+template <int OUT, int BM, int CW>
+__device__ __forceinline__ void stage_row_swizzled(uint8_t* staging, int r, int col_in_tile, const float (&acc)[CW]) {
+    using Tr = OutTraits<OUT>;
+    constexpr int ES = int(sizeof(typename Tr::T));
+#pragma unroll
+    for (int j = 0; j < CW; j += Tr::kVec) {
+        const int piece = (col_in_tile + j) * ES / 16;  // 16-byte piece of the tile row
+        const int box = piece >> 3, w = piece & 7;
+        uint8_t* dst = staging + box * (BM * 128) + r * 128 + ((w ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = pack16<OUT>(&acc[j]);
+    }
 }
 
 // Copy the staged BM x BN tile to `n_dst` outputs with identical row stride:
@@ -634,7 +656,12 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
             // Stage the tile, rounded to the output type, for the store warps.
             if (!take_staging()) break;
             const int b = handed % Cfg::SBUF;
-            stage_row<OUT, CW, Cfg::STAGE_PITCH>(staging + b * Cfg::STAGING_BYTES, q * 32 + lane, colg * CW, acc);
+            if (p.tma_store) {
+                stage_row_swizzled<OUT, BM, CW>(staging + b * Cfg::STAGING_BYTES, q * 32 + lane, colg * CW, acc);
+                fence_proxy_async_smem();  // the TMA store reads these bytes
+            } else {
+                stage_row<OUT, CW, Cfg::STAGE_PITCH>(staging + b * Cfg::STAGING_BYTES, q * 32 + lane, colg * CW, acc);
+            }
             const bool decide = inline_redo && main_item;
             if (decide && bad && lane == 0) atomicOr(&ctrl->tile_bad[b], 1);
             hand_over(tm, tn, decide ? kStoreDecide : kStoreTile);
@@ -672,8 +699,10 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
             const int4 m = ctrl->st_meta[b];
             if (m.z == kStoreEnd) break;
             const int tm = m.x, tn = m.y;
+            bool redo_queued = false;  // this main tile is redone later in this CTA
             if (m.z == kStoreDecide && sw == 0 && lane == 0) {
                 if (atomicExch(&ctrl->tile_bad[b], 0) != 0) {
+                    redo_queued = true;
                     const int tail = *rq_tail;
                     if (tail - *rq_head >= kRedoQueue) {
                         atomicCAS(p.status, 0, kStatusRedoQueueFull);
@@ -688,7 +717,22 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
                 *main_done = ++decided;
             }
             const uint8_t* stg = staging + b * Cfg::STAGING_BYTES;
-            if (p.c_vec)
+            if (p.tma_store) {
+                // One bulk tensor store per 128-byte column box.  A tile queued for
+                // its redo is not stored: the redo writes it, and two bulk stores
+                // to the same place are not ordered.
+                constexpr int BOX_COLS = 128 / Cfg::OUT_BYTES;
+                if (sw == 0 && lane == 0) {
+                    if (!redo_queued) {
+#pragma unroll
+                        for (int j = 0; j < BN / BOX_COLS; ++j)
+                            if (tn * BN + j * BOX_COLS < p.N)  // boxes wholly past the last column hold nothing
+                                tma_store_2d(&p.tmC, stg + j * (BM * 128), tn * BN + j * BOX_COLS, tm * BM);
+                        bulk_commit_group();
+                        bulk_wait_group_read0();  // the staging tile may be reused once read
+                    }
+                }
+            } else if (p.c_vec)
                 store_staged<OUT, BM, BN, Cfg::STAGE_PITCH, Cfg::STORE_WARPS>(
                     stg, dsts, 1 + p.n_peers, p.sCm, tm * BM, tn * BN, p.M, p.N, sw, lane, p.bias, p.sbias);
             else
@@ -697,7 +741,9 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
             __syncwarp();
             if (lane == 0) mbar_arrive(&ctrl->st_empty[b]);  // the staging tile is free again
         }
-        // peer stores become visible system-wide before the kernel is seen complete
+        // bulk stores complete, and peer stores become visible system-wide, before
+        // the kernel is seen complete
+        if (p.tma_store && sw == 0 && lane == 0) bulk_wait_group0();
         if (p.n_peers > 0) __threadfence_system();
     }
 
