@@ -287,8 +287,8 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
         p.bias = static_cast<const __half*>(bias);
         p.sbias = sbias;
         // Finished tiles leave through TMA stores when C allows (row-major, 16-byte
-        // aligned rows) and nothing else has to be written with them.
-        if (p.c_vec && n_peers == 0 && bias == nullptr) {
+        // aligned rows) and no peer copies have to be written with them.
+        if (p.c_vec && n_peers == 0) {
             const CUtensorMapDataType ct = c_dtype == F16ACC_OUT_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                            : c_dtype == F16ACC_OUT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;

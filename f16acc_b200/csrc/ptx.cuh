@@ -180,6 +180,18 @@ __device__ __forceinline__ void bulk_wait_group_read0() {
 }
 // Wait until every committed bulk store of this thread has completed.
 __device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// A read-only global FP16 load and a 16-byte shared store as volatile asm:
+// kept in program order with each other (bounds register live ranges).
+__device__ __forceinline__ __half ldg_half_ordered(const __half* p) {
+    unsigned short v;
+    asm volatile("ld.global.nc.b16 %0, [%1];" : "=h"(v) : "l"(p));
+    return __ushort_as_half(v);
+}
+__device__ __forceinline__ void st_shared_v4_ordered(void* p, uint4 v) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
 // Order this thread's generic-proxy shared-memory writes before later async-proxy
 // (TMA) accesses to them.
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -165,8 +165,13 @@ __device__ __forceinline__ void stage_row(uint8_t* staging, int row_in_tile, int
 // BN*sizeof(T)/128 boxes of BM rows x 128 bytes, each with the 128-byte
 // swizzle of the C tensor map (16-byte piece w of row r at position w ^ (r % 8)
 // of the row), which also spreads a warp's rows over all banks.
+// With `bias` (this thread's first column; element stride sbias, `ncols`
+// columns inside C) each value becomes add_bias of it, as the store warps'
+// copy-out computes it.  The bias loads and the staging stores are ordered
+// volatile asm, so only one piece's bias is live at a time.
 template <int OUT, int BM, int CW>
-__device__ __forceinline__ void stage_row_swizzled(uint8_t* staging, int r, int col_in_tile, const float (&acc)[CW]) {
+__device__ __forceinline__ void stage_row_swizzled(uint8_t* staging, int r, int col_in_tile, const float (&acc)[CW],
+                                                   const __half* bias, int64_t sbias, int ncols) {
     using Tr = OutTraits<OUT>;
     constexpr int ES = int(sizeof(typename Tr::T));
 #pragma unroll
@@ -174,13 +179,23 @@ __device__ __forceinline__ void stage_row_swizzled(uint8_t* staging, int r, int 
         const int piece = (col_in_tile + j) * ES / 16;  // 16-byte piece of the tile row
         const int box = piece >> 3, w = piece & 7;
         uint8_t* dst = staging + box * (BM * 128) + r * 128 + ((w ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = pack16<OUT>(&acc[j]);
+        float v[Tr::kVec];
+#pragma unroll
+        for (int i = 0; i < Tr::kVec; ++i) v[i] = acc[j + i];
+        if (bias != nullptr) {
+#pragma unroll
+            for (int i = 0; i < Tr::kVec; ++i)
+                if (j + i < ncols) v[i] = Tr::round_trip(v[i]) + __half2float(ldg_half_ordered(bias + (j + i) * sbias));
+        }
+        st_shared_v4_ordered(dst, pack16<OUT>(v));
     }
 }
 
 // Copy the staged BM x BN tile to `n_dst` outputs with identical row stride:
 // lanes run along a row, 16 bytes each, so every store instruction writes
-// whole contiguous row segments.  Column tails past N go element by element.
+// whole contiguous row segments.  Each lane reads U pieces from shared memory
+// before it stores them, so U loads are in flight at once.  Column tails past
+// N go element by element.
 template <int OUT, int BM, int BN, int PITCH, int NWARPS>
 __device__ __forceinline__ void store_staged(const uint8_t* staging, void* const* dst, int n_dst, int64_t sCm,
                                              int row0, int col0, int M, int N, int warp_idx, int lane,
@@ -188,26 +203,38 @@ __device__ __forceinline__ void store_staged(const uint8_t* staging, void* const
     using Tr = OutTraits<OUT>;
     using T = typename Tr::T;
     constexpr int kChunks = BN * int(sizeof(T)) / 16;  // 16-byte pieces per tile row
-    for (int idx = warp_idx * 32 + lane; idx < BM * kChunks; idx += NWARPS * 32) {
-        const int r = idx / kChunks, c16 = idx - r * kChunks;
-        const int grow = row0 + r, gcol = col0 + c16 * Tr::kVec;
-        if (grow >= M || gcol >= N) continue;
-        uint4 v = *reinterpret_cast<const uint4*>(staging + r * PITCH + c16 * 16);
-        if (bias != nullptr) v = add_bias16<OUT>(v, bias, sbias, gcol, N);
-        const int64_t off = int64_t(grow) * sCm + gcol;
-        if (gcol + Tr::kVec <= N) {
-            for (int d = 0; d < n_dst; ++d) *reinterpret_cast<uint4*>(reinterpret_cast<T*>(dst[d]) + off) = v;
-        } else {
-            const T* e = reinterpret_cast<const T*>(&v);
-            for (int d = 0; d < n_dst; ++d)
-                for (int t = 0; t < Tr::kVec && gcol + t < N; ++t) reinterpret_cast<T*>(dst[d])[off + t] = e[t];
+    constexpr int kStep = NWARPS * 32;
+    constexpr int kIters = BM * kChunks / kStep;
+    constexpr int U = 4;
+    static_assert(BM * kChunks % kStep == 0 && kIters % U == 0, "store split");
+    for (int it = 0; it < kIters; it += U) {
+        uint4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int idx = (it + u) * kStep + warp_idx * 32 + lane;
+            const int r = idx / kChunks, c16 = idx - r * kChunks;
+            v[u] = *reinterpret_cast<const uint4*>(staging + r * PITCH + c16 * 16);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int idx = (it + u) * kStep + warp_idx * 32 + lane;
+            const int r = idx / kChunks, c16 = idx - r * kChunks;
+            const int grow = row0 + r, gcol = col0 + c16 * Tr::kVec;
+            if (grow >= M || gcol >= N) continue;
+            uint4 x = v[u];
+            if (bias != nullptr) x = add_bias16<OUT>(x, bias, sbias, gcol, N);
+            const int64_t off = int64_t(grow) * sCm + gcol;
+            if (gcol + Tr::kVec <= N) {
+                for (int d = 0; d < n_dst; ++d) *reinterpret_cast<uint4*>(reinterpret_cast<T*>(dst[d]) + off) = x;
+            } else {
+                const T* e = reinterpret_cast<const T*>(&x);
+                for (int d = 0; d < n_dst; ++d)
+                    for (int t = 0; t < Tr::kVec && gcol + t < N; ++t) reinterpret_cast<T*>(dst[d])[off + t] = e[t];
+            }
         }
     }
 }
 
-// The same copy-out for outputs of any strides, one element per lane: lanes
-// run along a row when columns are contiguous (sCn == 1), else down a column,
-// which is the contiguous direction of a transposed C.
 template <int OUT, int BM, int BN, int PITCH, int NWARPS>
 __device__ __forceinline__ void store_staged_strided(const uint8_t* staging, void* const* dst, int n_dst, int64_t sCm,
                                                      int64_t sCn, int row0, int col0, int M, int N, int warp_idx,
@@ -657,7 +684,12 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
             if (!take_staging()) break;
             const int b = handed % Cfg::SBUF;
             if (p.tma_store) {
-                stage_row_swizzled<OUT, BM, CW>(staging + b * Cfg::STAGING_BYTES, q * 32 + lane, colg * CW, acc);
+                // The bias (if any) goes on here, after the flag, to the product
+                // rounded to the output type.
+                const int col0 = tn * BN + colg * CW;
+                stage_row_swizzled<OUT, BM, CW>(staging + b * Cfg::STAGING_BYTES, q * 32 + lane, colg * CW, acc,
+                                                p.bias != nullptr ? p.bias + int64_t(col0) * p.sbias : nullptr,
+                                                p.sbias, p.N - col0);
                 fence_proxy_async_smem();  // the TMA store reads these bytes
             } else {
                 stage_row<OUT, CW, Cfg::STAGE_PITCH>(staging + b * Cfg::STAGING_BYTES, q * 32 + lane, colg * CW, acc);
