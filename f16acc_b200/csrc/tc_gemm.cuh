@@ -14,20 +14,24 @@
 //   warp 0      tile scheduler and TMA producer: A [128 x 64] and B [BN x 64]
 //               (or [64 x BN] when B is N-contiguous) per stage into a 4-stage
 //               smem ring, 128-byte swizzle, completion counted on full[s].
-//   warps 1-2   MMA issuers (one lane each; warp 1 owns TMEM).  Chunked mode:
+//   warps 1-2   MMA warps (lane 0 issues; warp 1 owns TMEM).  Chunked mode:
 //               per 64-wide stage, the two 32-long chunks go to the two chunk
-//               buffers of a pair, warp 1 issuing chunk 0's two K=16
-//               tcgen05.mma kind::f16 (FP16 D, first with accumulate off) and
-//               warp 2 chunk 1's, each then tcgen05.commit -> tfull[pair].
-//               FP32 mode: warp 1 alone, the whole K loop into one FP32 buffer.
+//               buffers of a TMEM pair as two K=16 tcgen05.mma kind::f16 each
+//               (FP16 D, first with accumulate off), then one tcgen05.commit
+//               -> tfull[pair].  Hand-offs alternate between the pairs and
+//               between the two warps (warp 1 + b issues into pair b), and a
+//               pair is reclaimed with bar.sync on its named barrier.  FP32
+//               mode: warp 1 alone, the whole K loop into one FP32 buffer.
 //   warps 3..   epilogue, 4*EPI_SPLIT warps: warp w reads TMEM lanes
 //               32*(w%4).. (its lane quarter) and a CW = BN/EPI_SPLIT column
 //               slice.  Chunked mode: per pair tcgen05.ld (FP16 pairs packed),
-//               release the buffers, then one mixed-precision FP32 add per
-//               element into register accumulators; at tile end a non-finite
-//               probe sets the tile's flag bytes and the tile is staged in smem.
-//   last warp   store warp: copies each staged tile out to C (and the peers)
-//               and makes the in-kernel redo decisions.
+//               bar.arrive to release the pair, then one mixed-precision FP32
+//               add per element into register accumulators; at tile end a
+//               non-finite probe sets the tile's flag bytes and the tile is
+//               staged in smem (128-byte-swizzled boxes for the TMA store).
+//   last warp   store warp: writes each staged tile out (TMA bulk tensor
+//               stores, or plain stores to a strided C and to the peers) and
+//               makes the in-kernel redo decisions.
 // No cluster multicast anywhere; every load reads this GPU's own memory.
 #pragma once
 

@@ -191,6 +191,26 @@ def test_strided_outputs_through_the_c_abi(cuda):
         check_chunked(colmajor, a, b)
 
 
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16, torch.float32], ids=str)
+def test_padded_row_outputs_take_tma_stores(cuda, out_dtype):
+    # C is a 16-byte aligned column window of a wider buffer: the tcgen05 kernel
+    # writes it with TMA bulk stores through a tensor map of row stride 320
+    # elements.  M and N are not tile multiples, so the boxes are clipped at
+    # both edges; nothing outside the window may change.
+    g = torch.Generator().manual_seed(16)
+    a = torch.randn(200, 256, generator=g).half().to(cuda)
+    b = torch.randn(256, 168, generator=g).half().to(cuda)
+    ref, _ = mm_ex(a, b, out_dtype)
+    assert plan(a, b)["variant"] == _lib.VARIANT_TCGEN05
+    wide = torch.full((200, 320), -7.0, device=cuda, dtype=out_dtype)
+    col0 = 64  # 128 or 256 bytes into each row
+    out = wide[:, col0:col0 + 168]
+    mm_ex(a, b, out_dtype, out=out)
+    assert torch.equal(out, ref)
+    assert (wide[:, :col0] == -7).all() and (wide[:, col0 + 168:] == -7).all()
+    check_chunked(out, a, b)
+
+
 @pytest.mark.parametrize("variant", VARIANTS, ids=VNAMES.get)
 def test_fp32_accumulate_mode(cuda, variant):
     g = torch.Generator().manual_seed(7)
