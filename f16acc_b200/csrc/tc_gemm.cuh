@@ -171,7 +171,7 @@ __device__ __forceinline__ void stage_row(uint8_t* staging, int row_in_tile, int
 // of the row), which also spreads a warp's rows over all banks.
 // With `bias` (this thread's first column; element stride sbias, `ncols`
 // columns inside C) each value becomes add_bias of it, as the store warps'
-// copy-out computes it.  The bias loads and the staging stores are ordered
+// copy-out computes it; the bias loads and the staging stores are then ordered
 // volatile asm, so only one piece's bias is live at a time.
 template <int OUT, int BM, int CW>
 __device__ __forceinline__ void stage_row_swizzled(uint8_t* staging, int r, int col_in_tile, const float (&acc)[CW],
@@ -183,15 +183,16 @@ __device__ __forceinline__ void stage_row_swizzled(uint8_t* staging, int r, int 
         const int piece = (col_in_tile + j) * ES / 16;  // 16-byte piece of the tile row
         const int box = piece >> 3, w = piece & 7;
         uint8_t* dst = staging + box * (BM * 128) + r * 128 + ((w ^ (r & 7)) << 4);
-        float v[Tr::kVec];
-#pragma unroll
-        for (int i = 0; i < Tr::kVec; ++i) v[i] = acc[j + i];
-        if (bias != nullptr) {
+        if (bias == nullptr) {
+            *reinterpret_cast<uint4*>(dst) = pack16<OUT>(&acc[j]);
+        } else {
+            float v[Tr::kVec];
 #pragma unroll
             for (int i = 0; i < Tr::kVec; ++i)
-                if (j + i < ncols) v[i] = Tr::round_trip(v[i]) + __half2float(ldg_half_ordered(bias + (j + i) * sbias));
+                v[i] = j + i < ncols ? Tr::round_trip(acc[j + i]) + __half2float(ldg_half_ordered(bias + (j + i) * sbias))
+                                     : acc[j + i];
+            st_shared_v4_ordered(dst, pack16<OUT>(v));
         }
-        st_shared_v4_ordered(dst, pack16<OUT>(v));
     }
 }
 
@@ -657,9 +658,12 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
 #pragma unroll
                     for (int j = 0; j < CW; ++j) acc[j] = 0.0f;
                     if (!consume_chunk_pairs<CW>(acc, nchunks, pairs, abort_flag, p.status)) break;
-                    float z = 0.0f;
+                    // eight independent probe chains (a 64-long chain costs ~300 cycles of
+                    // latency at every tile end); NaN in any of them marks the tile
+                    float z8[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-                    for (int j = 0; j < CW; ++j) z = nonfinite_probe(z, acc[j]);
+                    for (int j = 0; j < CW; ++j) z8[j & 7] = nonfinite_probe(z8[j & 7], acc[j]);
+                    const float z = ((z8[0] + z8[1]) + (z8[2] + z8[3])) + ((z8[4] + z8[5]) + (z8[6] + z8[7]));
                     bad = __any_sync(0xffffffffu, z != z);
                     if (lane == 0) {
                         uint8_t* slot = p.flags + (static_cast<int64_t>(tm) * p.tiles_n + tn) * kFlagBytesPerTile;
