@@ -12,10 +12,18 @@ rotating over INPUT_SETS independent (A, B) pairs whose footprint exceeds the
 Multi-GPU (torchrun, one rank per GPU): M-sharded token batches are
 independent, so every rank runs the same per-GPU work on its own inputs with no
 collective on the data path ("scaling": "weak"); the time is the max over ranks.
+The line also carries `nshard`: BASELINE config 4c, the N-column-sharded
+16384^3 product whose GEMM kernel all-gathers C over NVLink as it runs, timed
+at this job's GPU count against the same product on one GPU.
 
 --impl reference times the reference's CPU path (the oracle restatement of
-steppergg/f16acc f16acc/kernel.py:37-81: chunked emulation) on the host cores,
-rank 0 only, on a bounded row sample of the same workload.
+steppergg/f16acc f16acc/kernel.py:37-81: chunked emulation, plus the FP64
+torch-CPU product of the same rows) on the host cores, rank 0 only, on a
+bounded row sample of the same workload.
+
+--workload selects the other BASELINE configs (shapes, overflow, nshard,
+prefill, decode) or one product shape timed alone (one), each printing its own
+JSON line.
 
 Prints one JSON line (rank 0).
 """
@@ -112,17 +120,38 @@ def barrier(torch, world: int):
 
 
 # ---------------------------------------------------------------- CPU baseline (oracle)
-def cpu_sample(rows: int, seed: int = 1):
+def cpu_operands(rows: int, seed: int = 1):
     import numpy as np
-
-    from oracle import oracle as O
 
     rng = np.random.default_rng(seed)
     scale = 4.0 / K ** 0.5
     a = (rng.standard_normal((rows, K)) * scale).astype(np.float16)
     b = (rng.standard_normal((K, N)) * scale).astype(np.float16)
+    return a, b
+
+
+def cpu_sample(rows: int, seed: int = 1):
+    """Seconds and TFLOPS of the oracle's chunked emulation of `rows` rows."""
+    from oracle import oracle as O
+
+    a, b = cpu_operands(rows, seed)
     t0 = time.perf_counter()
     O.gemm_chunked(a, b, round_every=32)
+    dt = time.perf_counter() - t0
+    return dt, 2.0 * rows * N * K / dt / 1e12
+
+
+def cpu_fp64_sample(rows: int, seed: int = 1):
+    """Seconds and TFLOPS of the FP64 torch-CPU product of the same rows (the
+    reference's accuracy oracle, tests/test_f16acc.py:22-29 `a.double() @
+    b.double()`), on the threads cpu_threads() set."""
+    import torch
+
+    a, b = cpu_operands(rows, seed)
+    a64 = torch.from_numpy(a).double()
+    b64 = torch.from_numpy(b).double()
+    t0 = time.perf_counter()
+    torch.mm(a64, b64)
     dt = time.perf_counter() - t0
     return dt, 2.0 * rows * N * K / dt / 1e12
 
@@ -130,20 +159,29 @@ def cpu_sample(rows: int, seed: int = 1):
 def cpu_threads():
     """Give the CPU path every host thread (torchrun pins OMP_NUM_THREADS=1)
     and report the count in effect."""
+    import torch
+
     from oracle import oracle as O
 
-    return O.set_threads(len(os.sched_getaffinity(0)) or os.cpu_count() or 1)
+    n = len(os.sched_getaffinity(0)) or os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return O.set_threads(n)
 
 
 def cpu_baseline(target_s: float = 10.0):
-    """Chunked emulation of rows of the 4096^3 product, sized to ~target_s."""
+    """The reference's CPU path on a bounded sample of the 4096^3 product: the
+    chunked emulation (the value) and the FP64 torch product, the same rows
+    each, on all host threads."""
     cores = cpu_threads()
     dt, _ = cpu_sample(16)
     rows = int(max(16, min(M, 16 * target_s / max(dt, 1e-3))))
     dt, tflops = cpu_sample(rows)
+    dt64, tflops64 = cpu_fp64_sample(rows)
     return {"value": tflops, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"oracle chunked emulation (oracle/f16acc_oracle.c, OpenMP) of {rows} of the 4096 rows "
-                      f"of one 4096^3 product: {dt:.1f} s"}
+            "sample": f"{rows} of the 4096 rows of one 4096^3 product: oracle chunked emulation "
+                      f"(oracle/f16acc_oracle.c, OpenMP) {dt:.1f} s; FP64 torch-CPU product {dt64:.2f} s",
+            "emulation_s": dt, "fp64_s": dt64, "fp64_tflops": tflops64, "rows": rows,
+            "torch_threads": __import__("torch").get_num_threads()}
 
 
 # ---------------------------------------------------------------- reference arm
@@ -164,6 +202,7 @@ def run_reference(args):
         times.append(dt)
     total = sum(times)
     value = args.steps * 2.0 * rows * N * K / total / 1e12
+    dt64, tflops64 = cpu_fp64_sample(rows)  # the reference's FP64 accuracy product, same rows
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
@@ -172,7 +211,10 @@ def run_reference(args):
                    "rows_per_step": rows},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": f"{rows} rows of the 4096^3 product per step (reference chunked semantics, "
-                                   "oracle/f16acc_oracle.c)"},
+                                   "oracle/f16acc_oracle.c); FP64 torch-CPU product of the same rows "
+                                   f"{dt64:.2f} s",
+                         "emulation_s": total / args.steps, "fp64_s": dt64, "fp64_tflops": tflops64,
+                         "torch_threads": __import__("torch").get_num_threads()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -275,11 +317,16 @@ def run_ours(args):
         cublas_f16 = time_torch(lambda i: torch.mm(*sets[i % INPUT_SETS], out=outs[i % INPUT_SETS]))
     finally:
         mmod.allow_fp16_accumulation = False
+    # the warp-level mma.sync variant (register accumulators, any strides) on the same
+    # products: the variant the tcgen05 kernel is measured against
+    mma_sync_tflops = time_torch(
+        lambda i: mm_ex(*sets[i % INPUT_SETS], torch.float16, True, variant=_lib.VARIANT_MMA_SYNC,
+                        out=outs[i % INPUT_SETS], workspace=wss[i % INPUT_SETS]), reps=GEMMS_PER_STEP)
 
     # ---- e2e through the public API with host buffers (pinned), copies inside the timed region.
     # Three streams: uploads of product i+1 and the download of product i-1 overlap product
     # i's kernel (PCIe is full duplex), as a serving loop would run them.
-    e2e_steps = max(1, min(args.steps, 3))
+    e2e_steps = args.steps
     host_in = [(a.cpu().pin_memory(), b.cpu().pin_memory()) for a, b in sets]
     host_out = [torch.empty(M, N, dtype=torch.float16).pin_memory() for _ in range(INPUT_SETS)]
     dev_in = [(torch.empty_like(a), torch.empty_like(b)) for a, b in sets]
@@ -324,6 +371,9 @@ def run_ours(args):
     h2d = GEMMS_PER_STEP * 2 * M * K * 2
     d2h = GEMMS_PER_STEP * M * N * 2
 
+    # ---- config 4c: the N-column-sharded 16384^3 product with its fused all-gather
+    nshard = measure_nshard(torch, world, rank, dev, peak)
+
     line = None
     if rank == 0:
         cpu = cpu_baseline() if world == 1 else None
@@ -351,7 +401,9 @@ def run_ours(args):
                            "streams so consecutive products overlap"},
             "gpu_launches": launches,
             "clocks": clocks.summary(),
+            "nshard": nshard,
             "context": {"cublas_f32acc_tflops": cublas_f32, "cublas_f16acc_tflops": cublas_f16,
+                        "mma_sync_tflops": mma_sync_tflops,
                         "reference_published": "65.7 TFLOPS f16acc at 4096^3 on RTX 4060 Ti (README.md:29)"},
         }
     if world > 1:
@@ -364,8 +416,98 @@ def run_ours(args):
     return 0
 
 
+NSHARD_N = 16384
+
+
+def measure_nshard(torch, world: int, rank: int, dev, peak: float, reps: int = 5) -> dict:
+    """BASELINE config 4c on this job's ranks: C = A @ B, 16384^3 fp16 N(0,1)
+    (seed 3, the same A and B on every rank), B column-sharded 1/world per
+    rank, each rank's GEMM storing its finished tiles into every rank's full C
+    over NVLink (shard.nshard_mm_fused; at one GPU the plain product).  Beside
+    it every rank times the unsharded product alone, the 1-GPU time the
+    speed-up is taken against.  Times are per product, max over ranks, CUDA
+    events around `reps` products after warm-up; the gathered C is checked
+    against FP64 on 64 sampled rows."""
+    from f16acc_b200.kernel import mm
+    from f16acc_b200.shard import nshard_mm_fused, shard_bounds
+
+    n = NSHARD_N
+    g = torch.Generator(device=dev).manual_seed(3)
+    a = torch.randn(n, n, device=dev, generator=g).half()
+    b = torch.randn(n, n, device=dev, generator=g).half()
+    lo, hi = shard_bounds(n, world, rank)
+    b_shard = b[:, lo:hi].contiguous()
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        barrier(torch, world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            r = fn()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier(torch, world)
+        return max_over_ranks(torch, e0.elapsed_time(e1) / reps, world, dev), r
+
+    ms_one, c = timed(lambda: mm(a, b))
+    if world > 1:
+        ms, c = timed(lambda: nshard_mm_fused(a, b_shard))
+    else:
+        ms = ms_one
+    rows = torch.randperm(n, generator=torch.Generator().manual_seed(7))[:64].to(dev)
+    ref = a[rows].double() @ b.double()
+    err = ((c[rows].double() - ref).abs().max() / ref.abs().max()).item()
+    err = max_over_ranks(torch, err, world, dev)
+    tflops = 2.0 * n ** 3 / (ms / 1e3) / 1e12
+    return {"workload": f"config 4c: {n}^3 fp16 N(0,1), B column-sharded over {world} GPU(s), "
+                        "fused GEMM + all-gather of C over NVLink (f16acc_gemm_allgather)",
+            "ms": ms, "tflops": tflops, "frac": tflops / (world * peak), "ms_1gpu_unsharded": ms_one,
+            "speedup_vs_1gpu": ms_one / ms, "max_rel_err_vs_fp64_64_rows": err, "reps": reps}
+
+
 def rel_err(x, ref) -> float:
     return ((x.double() - ref).abs().max() / ref.abs().max()).item()
+
+
+def one_product(args, dev):
+    """One product shape timed alone (`--workload one`): the small command the
+    ncu captures under profiles/ are taken with, since it launches little
+    besides the GEMM itself."""
+    import torch
+
+    from f16acc_b200 import _lib
+    from f16acc_b200.kernel import mm_ex, plan
+
+    m, n, k = (int(v) for v in args.shape.split(","))
+    g = torch.Generator(device=dev).manual_seed(1)
+    scale = 4.0 / k ** 0.5
+    a = (torch.randn(m, k, device=dev, generator=g) * scale).half()
+    if args.layout == "row_major":
+        b = (torch.randn(k, n, device=dev, generator=g) * scale).half()
+    else:
+        b = (torch.randn(n, k, device=dev, generator=g) * scale).half().t()
+    variant = {v: key for key, v in _lib.VARIANT_NAMES.items()}[args.variant]
+    out_dtype = {"f16": torch.float16, "f32": torch.float32}[args.out_dtype]
+    chunked = not args.fp32_acc
+    c, ws = mm_ex(a, b, out_dtype, chunked, variant=variant)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        mm_ex(a, b, out_dtype, chunked, variant=variant, out=c, workspace=ws)
+        e1.record()
+        times.append((e0, e1))
+    torch.cuda.synchronize()
+    med = statistics.median(e0.elapsed_time(e1) for e0, e1 in times)
+    ref = a.double() @ b.double()
+    return {"config": f"one product {m}x{n}x{k}, {args.layout} B, {args.out_dtype} out, "
+                      f"{'FP32' if args.fp32_acc else 'chunked FP16'} accumulate",
+            "kernel": _lib.VARIANT_NAMES[plan(a, b, variant)["variant"]], "median_ms": med,
+            "tflops": 2.0 * m * n * k / (med / 1e3) / 1e12, "max_rel_err_vs_fp64": rel_err(c, ref)}
 
 
 def run_workload(args):
@@ -453,6 +595,8 @@ def run_workload(args):
         flops = 2.0 * n ** 3
         line["results"] = {k: {"ms": v, "tflops": flops / v / 1e9} for k, v in times.items()}
         line["scaling"] = "strong"
+    elif args.workload == "one":
+        line.update(one_product(args, dev))
     elif args.workload == "prefill":
         r = W.prefill(dev, rank=rank, world=world)
         ms_c = max_over_ranks(torch, r["ms_cublas"], world, dev)
@@ -480,14 +624,19 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--variant", choices=["auto", "tcgen05", "mma_sync"], default="auto")
-    ap.add_argument("--workload", choices=["gemm4096", "shapes", "overflow", "nshard", "prefill", "decode"],
+    ap.add_argument("--variant", choices=["auto", "tcgen05", "mma_sync", "skinny"], default="auto")
+    ap.add_argument("--workload", choices=["gemm4096", "shapes", "overflow", "nshard", "prefill", "decode", "one"],
                     default="gemm4096",
                     help="gemm4096 is the headline line; the others print their own JSON line")
     ap.add_argument("--size", type=int, default=16384, help="matrix size for --workload nshard")
     ap.add_argument("--nshard-blocks", type=int, default=4, help="row blocks the sharded gather is pipelined in")
     ap.add_argument("--nshard-reserve", type=int, default=16, help="SMs left free for NCCL during the product")
     ap.add_argument("--nshard-sweep", action="store_true", help="also time the bare all-gather and other blockings")
+    ap.add_argument("--shape", default="4096,4096,4096", help="M,N,K for --workload one")
+    ap.add_argument("--layout", choices=["row_major", "w_t"], default="row_major", help="B layout, --workload one")
+    ap.add_argument("--out-dtype", choices=["f16", "f32"], default="f16", help="output type, --workload one")
+    ap.add_argument("--fp32-acc", action="store_true", help="--workload one: chunked=False (plain FP32 accumulate)")
+    ap.add_argument("--reps", type=int, default=10, help="timed products for --workload one")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)

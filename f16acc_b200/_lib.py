@@ -44,7 +44,7 @@ SIGNATURES = {
     "f16acc_set_redo_mode": (_int, [_int]),
     "f16acc_set_schedule": (_int, [_int]),
     "f16acc_probe_chunk_rate": (_int, [_int, _int, _int, _int, _p, _int, _p]),
-    "f16acc_probe_pair_trace": (_int, [_int, _int, _int, _int, _p, _p, _int, _p]),
+    "f16acc_selftest_wait_timeout": (_int, [ctypes.c_uint64, _p, _int, _p]),
     "f16acc_device_status": (_int, [_int, _int]),
     "f16acc_gemm_noalloc": (_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _int, _i64, _i64, _i64, _int,
                                    _int, _p]),

@@ -37,13 +37,28 @@ struct DeviceInfo {
 };
 DeviceInfo g_dev[kMaxDevices];
 
+// Per-device facts, looked up once.  The status word's address is resolved
+// with `device` current (cudaGetSymbolAddress answers for the current
+// device), whatever device the calling thread had selected; the caller's
+// device is restored afterwards.  nullptr for an ordinal that is not a
+// device of this process.
 DeviceInfo* device_info(int device) {
     if (device < 0 || device >= kMaxDevices) return nullptr;
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || device >= count) return nullptr;
     DeviceInfo* d = &g_dev[device];
     std::call_once(d->once, [d, device]() {
         d->err = cudaDeviceGetAttribute(&d->sms, cudaDevAttrMultiProcessorCount, device);
         if (d->err != cudaSuccess) return;
+        int prev = -1;
+        d->err = cudaGetDevice(&prev);
+        if (d->err != cudaSuccess) return;
+        if (prev != device && (d->err = cudaSetDevice(device)) != cudaSuccess) return;
         d->err = cudaGetSymbolAddress(reinterpret_cast<void**>(&d->status), g_status);
+        if (prev != device) {
+            const cudaError_t back = cudaSetDevice(prev);
+            if (d->err == cudaSuccess) d->err = back;
+        }
     });
     return d;
 }
@@ -451,10 +466,9 @@ int f16acc_get_plan(const void* A, int64_t sAm, int64_t sAk, const void* B, int6
 int f16acc_flag_bytes_per_tile(void) { return kFlagBytesPerTile; }
 
 int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void* out, int device, void* stream) {
-    const bool known = (mode >= 0 && mode <= 15 && mode != 5) || (mode >= 20 && mode <= 28) ||
-                       (mode >= 30 && mode <= 36) || (mode >= 40 && mode <= 43) || (mode >= 45 && mode <= 56);
+    const bool known = mode == 0 || mode == 1 || mode == 2 || mode == 30 || mode == 31 || mode == 32;
     if (!known || chunks < 0 || grid <= 0 || out == nullptr) return F16ACC_ERR_INVALID_ARGUMENT;
-    if (mode >= 2 && mode < 30 && epi_split != 2 && epi_split != 4) return F16ACC_ERR_INVALID_ARGUMENT;
+    if (mode == 2 && epi_split != 2 && epi_split != 4) return F16ACC_ERR_INVALID_ARGUMENT;
     DeviceInfo* info = device_info(device);
     if (!info) return F16ACC_ERR_INVALID_ARGUMENT;
     DeviceGuard guard(device);
@@ -465,17 +479,14 @@ int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void*
                : F16ACC_ERR_CUDA;
 }
 
-int f16acc_probe_pair_trace(int variant, int epi_split, int npairs, int grid, void* events, void* out, int device,
-                            void* stream) {
-    if (variant < 0 || variant > 4 || (epi_split != 2 && epi_split != 4) || npairs < 4 || grid <= 0 ||
-        events == nullptr || out == nullptr)
-        return F16ACC_ERR_INVALID_ARGUMENT;
+int f16acc_selftest_wait_timeout(uint64_t limit_ns, void* out, int device, void* stream) {
+    if (limit_ns == 0 || limit_ns > kWaitLimitNs || out == nullptr) return F16ACC_ERR_INVALID_ARGUMENT;
     DeviceInfo* info = device_info(device);
     if (!info) return F16ACC_ERR_INVALID_ARGUMENT;
     DeviceGuard guard(device);
     if (guard.err != cudaSuccess || info->err != cudaSuccess) return F16ACC_ERR_CUDA;
-    return launch_pair_trace(variant, epi_split, npairs, grid, static_cast<long long*>(events),
-                             static_cast<float*>(out), info->status, static_cast<cudaStream_t>(stream)) == cudaSuccess
+    return launch_wait_selftest(limit_ns, static_cast<unsigned long long*>(out), info->status,
+                                static_cast<cudaStream_t>(stream)) == cudaSuccess
                ? F16ACC_OK
                : F16ACC_ERR_CUDA;
 }

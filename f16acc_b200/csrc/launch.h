@@ -40,10 +40,14 @@ cudaError_t launch_skinny(const SkinnyParams& p, bool chunked, bool b_kn, int ou
 cudaError_t launch_fill_zero(void* C, int64_t sCm, int64_t sCn, int M, int N, int out, cudaStream_t stream,
                              const __half* bias = nullptr, int64_t sbias = 0);
 
-// Raw-rate probe (probes.cu): mode 0/1 MMA only with FP16/FP32 accumulator,
-// mode 2 the chunk pipeline; `out` holds grid * (64 + 128 * epi_split) floats.
+// Raw-rate probes (rate_probes.cu): mode 0/1 tcgen05 MMA only with an FP16 /
+// FP32 accumulator, mode 2 the chunk-pair pipeline, 30-32 warp-level mma.sync;
+// `out` holds grid * (96 + 128 * epi_split) floats (grid * 256 for 30-32).
 cudaError_t launch_chunk_rate(int mode, int epi_split, int chunks, int grid, float* out, int* status,
                               cudaStream_t stream);
+// Bounded-wait self-test (rate_probes.cu): one CTA whose waits run out after
+// limit_ns; out holds 3 values.
+cudaError_t launch_wait_selftest(uint64_t limit_ns, unsigned long long* out, int* status, cudaStream_t stream);
 
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per kernel and device.
 cudaError_t ensure_smem_attr_raw(const void* kernel, int smem);
@@ -51,11 +55,6 @@ template <typename Kernel>
 cudaError_t ensure_smem_attr(Kernel kernel, int smem) {
     return ensure_smem_attr_raw(reinterpret_cast<const void*>(kernel), smem);
 }
-
-// Timed pair pipeline (trace_probe.cu): `ev` holds npairs x 9 SM-clock stamps
-// from CTA 0, `out` grid * (64 + 128 * epi_split) floats.
-cudaError_t launch_pair_trace(int variant, int epi_split, int npairs, int grid, long long* ev, float* out,
-                              int* status, cudaStream_t stream);
 
 // Launch helper: cudaLaunchKernelEx with optional programmatic stream
 // serialisation (the dependent kernel may start its prologue while the

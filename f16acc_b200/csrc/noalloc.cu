@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <atomic>
 #include <mutex>
 
 #include "../../include/f16acc.h"
@@ -37,27 +38,28 @@ static __device__ __align__(256) uint8_t g_noalloc_flags[kNoAllocFlagBytes];
 
 constexpr int kMaxDevices = 64;
 
-struct NoAllocSlot {
-    std::once_flag once;
-    cudaError_t err = cudaSuccess;
-    void* ptr = nullptr;  // device address of g_noalloc_flags on this device
-};
-NoAllocSlot g_slots[kMaxDevices];
+// Device address of g_noalloc_flags, per device; nullptr until resolved.
+std::atomic<void*> g_scratch[kMaxDevices];
+std::mutex g_scratch_lock;
 
-// Once per device, with that device current: resolve the array's device address.
+// The array's device address on `device`, resolved with that device current
+// (the caller's device is restored).  A failed lookup is not remembered: the
+// next call tries again.
 void* scratch_for(int device) {
-    NoAllocSlot& s = g_slots[device];
-    std::call_once(s.once, [&s, device]() {
-        int prev = -1;
-        s.err = cudaGetDevice(&prev);
-        if (s.err != cudaSuccess) return;
-        if (prev != device && (s.err = cudaSetDevice(device)) != cudaSuccess) return;
-        void* p = nullptr;
-        s.err = cudaGetSymbolAddress(&p, g_noalloc_flags);
-        if (s.err == cudaSuccess) s.ptr = p;
-        if (prev != device) cudaSetDevice(prev);
-    });
-    return s.err == cudaSuccess ? s.ptr : nullptr;
+    void* p = g_scratch[device].load(std::memory_order_acquire);
+    if (p != nullptr) return p;
+    std::lock_guard<std::mutex> hold(g_scratch_lock);
+    p = g_scratch[device].load(std::memory_order_relaxed);
+    if (p != nullptr) return p;
+    int prev = -1;
+    if (cudaGetDevice(&prev) != cudaSuccess) return nullptr;
+    if (prev != device && cudaSetDevice(device) != cudaSuccess) return nullptr;
+    void* addr = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&addr, g_noalloc_flags);
+    if (prev != device && cudaSetDevice(prev) != cudaSuccess) return nullptr;
+    if (err != cudaSuccess) return nullptr;
+    g_scratch[device].store(addr, std::memory_order_release);
+    return addr;
 }
 
 }  // namespace
@@ -66,10 +68,17 @@ void* scratch_for(int device) {
 extern "C" int f16acc_gemm_noalloc(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int64_t sBn,
                                    void* C, int64_t sCm, int64_t sCn, int c_dtype, int64_t M, int64_t N, int64_t K,
                                    int chunked, int device, void* stream) {
+    int count = 0;
     if (device < 0 || device >= f16acc::kMaxDevices) return F16ACC_ERR_INVALID_ARGUMENT;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || device >= count) return F16ACC_ERR_INVALID_ARGUMENT;
     if (M < 0 || N < 0 || K < 0) return F16ACC_ERR_INVALID_ARGUMENT;
+    // The flags are only read and written by a chunked product with work to do;
+    // every other call is f16acc_gemm without a workspace.
+    if (!chunked || M == 0 || N == 0 || K == 0)
+        return f16acc_gemm(A, sAm, sAk, B, sBk, sBn, C, sCm, sCn, c_dtype, M, N, K, chunked, nullptr, 0, device,
+                           stream);
     const size_t need = f16acc_workspace_bytes(M, N, K);
-    if (chunked && need > f16acc::kNoAllocFlagBytes) return F16ACC_ERR_TOO_LARGE;
+    if (need > f16acc::kNoAllocFlagBytes) return F16ACC_ERR_TOO_LARGE;
     void* flags = f16acc::scratch_for(device);
     if (flags == nullptr) return F16ACC_ERR_CUDA;
     return f16acc_gemm(A, sAm, sAk, B, sBk, sBn, C, sCm, sCn, c_dtype, M, N, K, chunked, flags,

@@ -18,7 +18,7 @@ enum DeviceStatus : int {
     kStatusTimeoutProducer = 0x101,   // TMA producer waited too long for a free smem stage
     kStatusTimeoutMma = 0x102,        // MMA warp waited too long for data or a free TMEM buffer
     kStatusTimeoutEpilogue = 0x103,   // epilogue waited too long for an accumulator
-    kStatusTimeoutProbe = 0x104,      // a probe kernel's wait ran out
+    kStatusTimeoutProbe = 0x104,      // a probe or self-test kernel's wait ran out
     kStatusTimeoutSchedule = 0x105,   // the tile scheduler waited too long for the epilogue's flag decisions
     kStatusRedoQueueFull = 0x106,     // in-kernel redo queue overflow (a bug; the kernel stops)
     kStatusTimeoutStore = 0x107,      // store warps waited too long for a staged tile
@@ -65,50 +65,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete.  Bounded: gives up
-// after kWaitLimitNs, or at once when another thread of the CTA has already
+// after limit_ns (kWaitLimitNs in every product kernel; the wait self-test
+// passes a short one), or at once when another thread of the CTA has already
 // given up (*abort != 0).  On giving up it records `code` in *status and
 // sets *abort.  Returns false when it gave up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
-                                          int code) {
+                                          int code, uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 63u) == 0u) {
             if (*abort) return false;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                atomicCAS(status, 0, code);
-                *abort = 1;
-                return false;
-            }
-        }
-    }
-}
-
-// Non-blocking test of a phase (no suspend), for spin loops.
-__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return done != 0;
-}
-
-// mbar_wait with a pure spin on test_wait (lower wake-up latency, costs issue
-// slots while waiting).  Same bounds and abort behaviour.
-__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
-                                               int code) {
-    if (mbar_test_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_test_wait(bar, parity)) return true;
-        if ((i & 1023u) == 0u) {
-            if (*abort) return false;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (globaltimer_ns() - t0 > limit_ns) {
                 atomicCAS(status, 0, code);
                 *abort = 1;
                 return false;

@@ -6,9 +6,11 @@ signature, the same ValueError checks and messages, C allocated here with
 `out_dtype`, a per-call flag workspace from the caching allocator, and an
 asynchronous launch on the current stream with no host sync.  The work itself
 is the native library (include/f16acc.h): a warp-specialised tcgen05/TMA
-kernel when the operands allow TMA, else a warp-level mma.sync kernel that
-takes any strides; tiles whose FP16 chunk overflowed are redone with FP32
-accumulation by a second kernel launched behind the first on the stream.
+kernel when the operands allow TMA, a few-row kernel for M <= 64, else a
+warp-level mma.sync kernel that takes any strides.  Tiles whose FP16 chunk
+overflowed are redone with FP32 accumulation on the device: inside the same
+tcgen05 launch by default, otherwise by a second kernel launched behind the
+first on the stream.
 
 Unlike the reference there is no autotuner state: the kernel choice is a pure
 function of the operands, so `mm` may be called from several threads.

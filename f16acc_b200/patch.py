@@ -1,15 +1,18 @@
-"""Route FP16 nn.Linear through the chunked FP16-accumulate GEMM.
+"""Linear-layer routing: `enable()` makes every qualifying torch linear call
+run on the chunked GEMM of this package; `disable()` puts cuBLAS back.
 
-    import f16acc_b200 as f16acc; f16acc.enable()
-
-Behaviour of steppergg/f16acc f16acc/patch.py:17-40, kept as is: only
-F.linear is replaced (every nn.Linear calls it).  Inputs that are not fp16 on
-CUDA, need gradients, or have fewer than MIN_ROWS rows (token-by-token
-decode, memory bound) go to the original F.linear (cuBLAS).  FP16 chunk
-overflow is handled on the device (the tile is redone with FP32 accumulation),
-so there is no host sync per call.  An fp16 bias of shape (out_features,) is
-added inside the GEMM's epilogue instead of the reference's separate `y += b`
-pass (same bits); any other bias takes the reference's in-place add.
+The hook point is `torch.nn.functional.linear`, the function nn.Linear's
+forward looks up at call time, so patching that one attribute covers every
+nn.Linear in every model.  The routing rule is the reference's
+(steppergg/f16acc f16acc/patch.py:22-32, kept unchanged for drop-in
+behaviour): a call is routed only when the input is fp16 on a CUDA device,
+the weight is fp16, no autograd graph is being recorded, and the flattened
+input has at least MIN_ROWS rows; anything else (CPU tensors, other dtypes,
+training, few-row decode steps) goes to the saved original.  Overflowing
+tiles are repaired on the device, so a routed call never synchronises with
+the host.  One change from the reference: an fp16 bias of shape
+(out_features,) is applied by the GEMM's epilogue instead of by a second
+in-place pass over the output; the bits are the same.
 """
 
 import torch
@@ -41,7 +44,7 @@ def linear(x, w, b=None):
 
 
 def enable():
-    F.linear = linear  # nn.Linear calls F.linear through this same module
+    F.linear = linear  # the attribute nn.Linear.forward resolves on every call
 
 
 def disable():

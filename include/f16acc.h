@@ -199,53 +199,29 @@ int f16acc_set_redo_mode(int mode);
 #define F16ACC_SCHEDULE_DYNAMIC 1
 int f16acc_set_schedule(int mode);
 
-/* Raw-rate probe, the B200 counterpart of the reference's bench/rate.py and
- * bench/chunkrate.py: `grid` CTAs (one per SM) each run `chunks` 32-long
- * chunks of 128x128 tcgen05 MMAs on a fixed shared-memory tile.  mode 0: MMA
- * only, FP16 accumulator; mode 1: MMA only, FP32 accumulator; mode 2: the
- * GEMM kernel's chunk pipeline (MMA + TMEM load + FP32 add per element) with
- * epi_split 2 or 4.  Breakdown modes: 3 = mode 2 without the adds, 4 = the
- * MMA/epilogue hand-off alone (no TMEM loads), 6 = TMEM loads alone (no MMA,
- * no hand-off), 7 = TMEM loads + adds (no MMA).  Latency modes (one thread:
- * an MMA group, commit, wait): 8 = 2 MMAs N=128, 9 = 1 MMA N=128, 10 = 2 MMAs
- * N=64, 11 = 8 MMAs N=128.  Spinning-wait variants: 12 = mode 2, 13 = mode 4,
- * 15 = barrier ping-pong without MMAs (14 = the same with suspending waits),
- * 20 = the ping-pong with 8 slots.  21 / 22 = MMA only with N=64 / N=256
- * instructions; 23 = chunk pipeline whose epilogue warps issue the next
- * chunk's MMAs themselves after a named barrier.  24 / 25 / 26 = ping-pong
- * without tcgen05 fences / with per-thread arrives / both; 27 = mode 4 with
- * per-thread arrives; 28 = MMA issue with a commit per chunk, no waiting;
- * 40 = chunk pipeline handing chunks over in pairs (one commit / release per
- * two chunks); 41 = chunk pipeline with 16 epilogue warps, two per (lane
- * quarter, column slice) taking alternate chunks (epi_split 4); 42 / 43 =
- * pairs with 16 epilogue warps, plain / software pipelined (epi_split 4);
- * 45 = 128x256 chunks (N=256 MMAs, 2 TMEM buffers), 16 epilogue warps;
- * 46 = pairs handed over per N-half (N=64 MMAs, one commit per half),
- * 16 epilogue warps.
- * Warp-level mma.sync rate (grid blocks of 8
- * warps, 8 m16n8k16 chains per warp, `chunks` iterations): 30 = FP16
- * accumulate, 31 = FP32 accumulate, 32 = FP16 chunks of 2 steps added into FP32;
- * 33 / 34 = fed from shared memory by ldmatrix, 64x64 warp tiles, with / without
- * the FP32 adds (one block of 8 warps per SM); 35 / 36 = the same issuing each
- * group of 8 / 16 tiles' first K16 MMAs before their second ones.
- * `out` is device memory for grid * max(256, 64 + 128*epi_split) floats.
- * Asynchronous on `stream`; time it with events. */
+/* Raw-rate probes, the B200 counterparts of the reference's bench/rate.py and
+ * bench/chunkrate.py (measurement aids).  tcgen05 modes: `grid` CTAs (one per
+ * SM) each run `chunks` 32-long chunks of 128x128 MMAs on a fixed
+ * shared-memory tile; mode 0 = MMA only, FP16 accumulator; 1 = MMA only, FP32
+ * accumulator; 2 = the GEMM kernel's chunk-pair pipeline (MMA + TMEM load +
+ * one FP32 add per element) with epi_split 2 or 4 (8 or 16 epilogue warps).
+ * Warp-level mma.sync modes (`grid` blocks of 8 warps, `chunks` iterations of
+ * 8 independent m16n8k16 products per warp on register operands): 30 = FP16
+ * accumulate, 31 = FP32 accumulate, 32 = FP16 chunks of two K16 steps added
+ * into FP32.  `out` is device memory for grid * (96 + 128 * epi_split) floats
+ * (grid * 256 for modes 30-32).  Asynchronous on `stream`; time it with
+ * events. */
 int f16acc_probe_chunk_rate(int mode, int epi_split, int chunks, int grid, void *out, int device, void *stream);
 
-/* Timed chunk-pair hand-off (a measurement tool): the pair pipeline of the
- * chunked kernel without global operands, `npairs` pairs on `grid` CTAs of
- * 2 + 4*epi_split warps, with SM-clock stamps of every step written by CTA 0
- * to `events` (device memory, npairs x 9 int64: MMA warp woke, after its
- * fence, first MMA issued, fourth MMA issued, commit issued, epilogue warp 0
- * woke and released, last epilogue warp woke and released).  variant 0 = the
- * product's hand-off, 1 = without the FP32 adds, 2 = the MMA warp alone
- * (no waits; only its five stamps are written), 3 = as 0 with two MMA threads
- * (one per chunk of a pair; the stamps are the first one's), 4 = as 3 with
- * the epilogue warps of the two issuing sub-partitions starting their adds
- * only after their MMA thread has issued the next pair.  `out` holds
- * grid * (64 + 128*epi_split) floats. */
-int f16acc_probe_pair_trace(int variant, int epi_split, int npairs, int grid, void *events, void *out, int device,
-                            void *stream);
+/* Self-test of the bounded waits every kernel here uses (no counterpart in
+ * the reference): one CTA waits on a barrier that nothing arrives on, gives up
+ * after limit_ns nanoseconds (0 < limit_ns <= 4e9), records status 0x104 in
+ * the device status word and stops the CTA's other waiters through its abort
+ * flag, as a product kernel does when a wait runs out.  `out` is device memory
+ * for 3 uint64: the nanoseconds waited, the number of other waiters (64) that
+ * left on the abort flag, and 1 if the wait wrongly reported success.  The
+ * status word stays set until f16acc_device_status(device, 1) resets it. */
+int f16acc_selftest_wait_timeout(uint64_t limit_ns, void *out, int device, void *stream);
 
 /* Device status word: 0, or the code of the first wait a kernel on `device`
  * gave up on since the last reset.  Synchronises the device.  reset != 0
@@ -262,10 +238,15 @@ int f16acc_device_status(int device, int reset);
  * synchronise the device and can fail under memory pressure).
  * Limit: a chunked call whose output needs more than F16ACC_NOALLOC_MAX_TILES
  * tiles (e.g. beyond 32768 x 32768) returns F16ACC_ERR_TOO_LARGE without
- * launching.  The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress) and must come before any stream capture on that
- * device.  All calls share the array: calls whose work overlaps on the GPU
- * (other streams, other host threads) race and must be serialised. */
+ * launching.  The first chunked call on a device looks up the array's device
+ * address (cudaGetSymbolAddress, with that device current) and must come
+ * before any stream capture on that device.  All calls share the array, which
+ * keeps the last call's flags; nothing needs clearing, because every chunked
+ * main pass rewrites all flag bytes of the tiles it covers before they are
+ * read.  Calls whose work overlaps on the GPU (other streams, other host
+ * threads) race on the array and must be serialised.  After a kernel gave up
+ * on a wait (f16acc_device_status non-zero) the output of that call and the
+ * array's flags are undefined until the status word is reset. */
 #define F16ACC_NOALLOC_MAX_TILES 65536
 int f16acc_gemm_noalloc(const void *A, int64_t sAm, int64_t sAk,
                         const void *B, int64_t sBk, int64_t sBn,

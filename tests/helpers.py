@@ -37,3 +37,23 @@ def chunk_ulp_bound(a16, b16, ulps=2.0, chunk=32):
         bound += ulps * ulp16(absum)
     nch = max(1, (K + chunk - 1) // chunk)
     return bound + nch * run * 2.0 ** -23 + 1e-30
+
+
+def chunk_ulp_bound_torch(a16, b16, ulps=2.0, chunk=32):
+    """chunk_ulp_bound computed on the operands' device in float64 (torch
+    tensors [M, K] and [K, N], any strides): the same bound for products too
+    large for a numpy loop over the chunks."""
+    import torch
+
+    a = a16.double().abs()
+    b = b16.double().abs()
+    K = a.shape[1]
+    bound = torch.zeros(a.shape[0], b.shape[1], dtype=torch.float64, device=a.device)
+    run = torch.zeros_like(bound)
+    for k0 in range(0, K, chunk):
+        absum = a[:, k0:k0 + chunk] @ b[k0:k0 + chunk]
+        run += absum
+        e = torch.floor(torch.log2(torch.clamp(absum, min=2.0 ** -14)))
+        bound += ulps * torch.exp2(e - 10)
+    nch = max(1, (K + chunk - 1) // chunk)
+    return bound + nch * run * 2.0 ** -23 + 1e-30

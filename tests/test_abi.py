@@ -53,6 +53,19 @@ def test_invalid_arguments_rejected_before_any_cuda_call():
     assert lib.f16acc_gemm(None, 0, 0, None, 0, 0, None, 0, 0, 0, 5, 0, 5, 1, None, 0, 0, None) == _lib.OK
 
 
+def test_device_ordinals_that_are_not_devices_are_invalid_arguments():
+    # ordinal 63 is below the library's table size but no device of this
+    # process (none at all on a CPU-only host)
+    lib = _lib.load()
+    assert lib.f16acc_gemm(None, 0, 0, None, 0, 0, None, 0, 0, 0, 5, 5, 5, 1, None, 0, 63, None) == \
+        _lib.ERR_INVALID_ARGUMENT
+    assert lib.f16acc_gemm_noalloc(None, 0, 0, None, 0, 0, None, 0, 0, 0, 5, 5, 5, 1, 63, None) == \
+        _lib.ERR_INVALID_ARGUMENT
+    assert lib.f16acc_gemm_noalloc(None, 0, 0, None, 0, 0, None, 0, 0, 0, 5, 5, 5, 1, -1, None) == \
+        _lib.ERR_INVALID_ARGUMENT
+    assert lib.f16acc_device_status(63, 0) == -1
+
+
 def test_plan_without_a_gpu_is_mma_sync_or_tcgen05():
     p = _lib.Plan()
     rc = _lib.load().f16acc_get_plan(16, 64, 1, 16, 1, 64, 128, 128, 64, _lib.VARIANT_MMA_SYNC, p)

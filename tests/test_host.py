@@ -16,6 +16,26 @@ def test_public_surface_is_the_reference_one():
     assert patch._orig is torch.nn.functional.linear or patch._orig.__name__ == "linear"
 
 
+def test_reference_import_name_is_the_same_package():
+    # `import f16acc` / `from f16acc import patch` (tests/test_f16acc.py:5-6)
+    # give this build's objects, not copies: state is shared both ways
+    import importlib
+
+    ref_name = importlib.import_module("f16acc")
+    ref_kernel = importlib.import_module("f16acc.kernel")
+    from f16acc import patch as ref_patch
+
+    assert ref_name.__all__ == ["mm", "enable", "disable", "calls"]
+    assert ref_patch is patch and ref_name.calls is patch.calls
+    assert ref_name.mm is f16acc.mm and ref_kernel.mm is f16acc.mm
+    ref_name.enable()
+    try:
+        assert torch.nn.functional.linear is patch.linear
+    finally:
+        ref_name.disable()
+    assert torch.nn.functional.linear is patch._orig
+
+
 def test_mm_rejects_bad_inputs_with_valueerror():
     a = torch.randn(256, 64).half()
     for bad in (torch.randn(32, 64).half(), torch.randn(64, 64), torch.randn(64, 64).half()):

@@ -1,11 +1,13 @@
 """The reference's own test suite (steppergg/f16acc tests/test_f16acc.py),
-re-run against this build: same inputs, same thresholds, same API calls."""
+re-run against this build: same inputs, same thresholds, same API calls, and
+the reference's own imports (`import f16acc`, `from f16acc import patch`,
+tests/test_f16acc.py:5-6), which resolve to this build's drop-in package."""
 
 import pytest
 import torch
 
-import f16acc_b200 as f16acc
-from f16acc_b200 import patch
+import f16acc
+from f16acc import patch
 
 pytestmark = pytest.mark.gpu
 

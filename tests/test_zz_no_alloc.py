@@ -43,6 +43,20 @@ def _reference(lib, a, b, out_dtype, chunked):
     return c
 
 
+def _flagged_tiles(lib, a, b):
+    """Tiles the allocating entry point flags for these operands (its own,
+    freshly allocated workspace)."""
+    M, K = a.shape
+    N = b.shape[1]
+    c = torch.empty(M, N, device=a.device, dtype=torch.float32)
+    ws = torch.empty(lib.f16acc_workspace_bytes(M, N, K), device=a.device, dtype=torch.uint8)
+    rc = lib.f16acc_gemm(a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(), b.stride(0), b.stride(1),
+                         c.data_ptr(), c.stride(0), c.stride(1), _lib.OUT_F32, M, N, K, 1, ws.data_ptr(),
+                         ws.numel(), a.device.index or 0, torch.cuda.current_stream(a.device).cuda_stream)
+    assert rc == _lib.OK
+    return int(ws.view(-1, 16).ne(0).any(dim=1).sum())
+
+
 def _noalloc(lib, a, b, out_dtype, chunked, out=None):
     M, K = a.shape
     N = b.shape[1]
@@ -88,6 +102,36 @@ def test_noalloc_fp32_accumulate_and_other_shapes(cuda):
                 assert rc == _lib.OK
                 torch.cuda.synchronize()
                 assert torch.equal(c, ref)
+
+
+@pytest.mark.parametrize("redo", ["inline", "separate"])
+@pytest.mark.parametrize("M", [512, 16], ids=["tcgen05", "few_rows"])
+def test_noalloc_overflow_then_clean_inputs(cuda, redo, M):
+    # The shared array still holds the first call's set flags when the second,
+    # clean call of the same shape runs: every one of them must be rewritten,
+    # or the second call would redo (and differ on) tiles it never flagged.
+    # M = 16 takes the few-row kernel, which writes its flags per column tile.
+    lib = _lib.load()
+    g = torch.Generator().manual_seed(21 + M)
+    N, K = 640, 384
+    bad_a = torch.randn(M, K, generator=g)
+    bad_b = torch.randn(K, N, generator=g)
+    bad_a[torch.randperm(M, generator=g)[: max(1, M // 64)]] *= 256.0
+    bad_b[:, torch.randperm(N, generator=g)[: N // 64]] *= 256.0
+    bad = (bad_a.half().to(cuda), bad_b.half().to(cuda))
+    clean = (torch.randn(M, K, generator=g).half().to(cuda), torch.randn(K, N, generator=g).half().to(cuda))
+    mode = {"inline": _lib.REDO_INLINE, "separate": _lib.REDO_SEPARATE}[redo]
+    prev = lib.f16acc_set_redo_mode(mode)
+    try:
+        assert _flagged_tiles(lib, *bad) > 0 and _flagged_tiles(lib, *clean) == 0
+        for a, b in (bad, clean, bad, clean):
+            ref = _reference(lib, a, b, torch.float32, True)
+            rc, c = _noalloc(lib, a, b, torch.float32, True)
+            assert rc == _lib.OK, _lib.strerror(rc)
+            torch.cuda.synchronize()
+            assert torch.equal(c, ref)
+    finally:
+        lib.f16acc_set_redo_mode(prev)
 
 
 def test_noalloc_rejects_outputs_beyond_its_fixed_array(cuda):
