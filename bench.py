@@ -274,9 +274,13 @@ def run_ours(args):
     value = gemms_total * flops_per_gemm() / (ms_max / 1e3) / 1e12
     launches = args.steps * GEMMS_PER_STEP  # one kernel per product
 
-    # ---- roofline: the kernel's own duration, one event pair per launch
+    # ---- roofline: the kernel's own duration, one event pair per launch.  A device-side
+    # sleep first holds the stream while the launches are queued behind it, so no
+    # interval includes host time spent issuing the next launch.
     n_main = min(64, max(16, args.steps * 2))
     main_ms = []
+    torch.cuda.synchronize()
+    torch.cuda._sleep(40_000_000)  # ~20 ms of SM clock cycles
     for i in range(n_main):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)

@@ -37,7 +37,7 @@ constexpr int kProbeSmem = 200 * 1024;
 
 struct ProbeCtrl {
     uint64_t tfull[2];
-    uint64_t done;
+    uint64_t done[2];  // one per MMA-issuing warp: its MMAs have completed
     uint32_t tmem_slot;
     int abort_flag;
 };
@@ -60,7 +60,8 @@ __global__ void __launch_bounds__(96 + 128 * EPI_SPLIT, 1) tc_rate_kernel(int ch
     if (threadIdx.x == 0) {
         mbar_init(&ctrl->tfull[0], 1);
         mbar_init(&ctrl->tfull[1], 1);
-        mbar_init(&ctrl->done, 1);
+        mbar_init(&ctrl->done[0], 1);
+        mbar_init(&ctrl->done[1], 1);
         ctrl->abort_flag = 0;
         fence_mbarrier_init();
     }
@@ -84,8 +85,8 @@ __global__ void __launch_bounds__(96 + 128 * EPI_SPLIT, 1) tc_rate_kernel(int ch
 #pragma unroll
                 for (int h = 0; h < 2; ++h) umma_f16(d, adesc(2 * (c & 1) + h), bdesc(2 * (c & 1) + h), idesc, h);
             }
-            umma_commit(&ctrl->done);
-            mbar_wait_drain(&ctrl->done, 0);
+            umma_commit(&ctrl->done[0]);
+            mbar_wait_drain(&ctrl->done[0], 0);
         }
     } else if (warp == 1 || warp == 2) {
         // MMA warp 1 + b issues hand-offs b, b + 2, ... into pair b and reclaims the
@@ -117,8 +118,8 @@ __global__ void __launch_bounds__(96 + 128 * EPI_SPLIT, 1) tc_rate_kernel(int ch
         }
         if (pending && !stopped && !aborted()) named_bar_sync(kPairBarrier + int(mine), NB);
         if (lane == 0) {
-            umma_commit(&ctrl->done);
-            mbar_wait_drain(&ctrl->done, 0);
+            umma_commit(&ctrl->done[mine]);
+            mbar_wait_drain(&ctrl->done[mine], 0);
         }
         __syncwarp();
     } else if (warp >= FIRST_EPI && warp < FIRST_EPI + EPI_WARPS) {

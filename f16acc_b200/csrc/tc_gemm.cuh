@@ -478,7 +478,15 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
             const bool issue = lane == 0;
             constexpr uint32_t idesc = idesc_f16(!CHUNKED, B_MN, BM, BN);
             constexpr uint32_t idesc32 = idesc_f16(true, B_MN, BM, BN);
-            const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
+            // Operand descriptors of stage 0.  Stage s and K16 step ks are reached by
+            // adding their byte offset / 16 to the start-address field, which cannot
+            // carry out (shared addresses stay below 2^18), so the issue loop spends
+            // one add per descriptor.
+            const uint64_t a_desc0 = sdesc_sw128(smem_u32(sA), 16, 1024);
+            const uint64_t b_desc0 = B_MN ? sdesc_sw128(smem_u32(sB), 64 * BK * 2, 1024)
+                                          : sdesc_sw128(smem_u32(sB), 16, 1024);
+            constexpr uint32_t kAStage = Cfg::A_BYTES >> 4, kBStage = Cfg::B_BYTES >> 4;
+            constexpr uint32_t kAStep = 32 >> 4, kBStep = (B_MN ? 2048 : 32) >> 4;  // one K16 step
             uint32_t s = 0, ph = 0, b = 0, tph = 0;
             bool pending = false;  // chunked: a hand-off issued into `mine` and not yet reclaimed
             // A bounded mbarrier wait, uniform across the warp in the chunked kernel.
@@ -509,15 +517,12 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
                     if (!wait(&full[s], ph)) return false;
                     tc_fence_after();
                     if (issue) {
+                        const uint64_t a_st = a_desc0 + s * kAStage, b_st = b_desc0 + s * kBStage;
 #pragma unroll
                         for (int ks = 0; ks < BK / 16; ++ks) {
                             const int k16 = kb * (BK / 16) + ks;
                             if (k16 >= nk16) break;
-                            const uint64_t ad = sdesc_sw128(sA0 + s * Cfg::A_BYTES + ks * 32, 16, 1024);
-                            const uint64_t bd = B_MN
-                                                    ? sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 2048, 64 * BK * 2, 1024)
-                                                    : sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 32, 16, 1024);
-                            umma_f16(d, ad, bd, idesc32, k16 > 0 ? 1u : 0u);
+                            umma_f16(d, a_st + ks * kAStep, b_st + ks * kBStep, idesc32, k16 > 0 ? 1u : 0u);
                         }
                         umma_commit(&empty[s]);
                     }
@@ -562,20 +567,26 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
                             if (!reclaim()) goto mma_done;
                             tc_fence_after();
                             if (issue) {
+                                const uint64_t a_st = a_desc0 + s * kAStage, b_st = b_desc0 + s * kBStage;
+                                const uint32_t d0 = tmem + (2 * b) * Cfg::ACC_COLS;
+                                if ((kb + 1) * BK <= p.K) {
+                                    // a whole stage: chunk 2kb into buffer 2b, chunk 2kb+1 into 2b+1
+                                    umma_f16(d0, a_st, b_st, idesc, 0u);
+                                    umma_f16(d0, a_st + kAStep, b_st + kBStep, idesc, 1u);
+                                    umma_f16(d0 + Cfg::ACC_COLS, a_st + 2 * kAStep, b_st + 2 * kBStep, idesc, 0u);
+                                    umma_f16(d0 + Cfg::ACC_COLS, a_st + 3 * kAStep, b_st + 3 * kBStep, idesc, 1u);
+                                } else {
 #pragma unroll
-                                for (int cc = 0; cc < 2; ++cc) {
-                                    const int c = kb * 2 + cc;
-                                    if (c >= nchunks) break;
-                                    const uint32_t d = tmem + (2 * b + cc) * Cfg::ACC_COLS;
+                                    for (int cc = 0; cc < 2; ++cc) {
+                                        const int c = kb * 2 + cc;
+                                        if (c >= nchunks) break;
 #pragma unroll
-                                    for (int h = 0; h < 2; ++h) {
-                                        const int ks = cc * 2 + h;
-                                        if (h == 1 && c * 32 + 16 >= p.K) break;  // K16 step past the end adds nothing
-                                        const uint64_t ad = sdesc_sw128(sA0 + s * Cfg::A_BYTES + ks * 32, 16, 1024);
-                                        const uint64_t bd =
-                                            B_MN ? sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 2048, 64 * BK * 2, 1024)
-                                                 : sdesc_sw128(sB0 + s * Cfg::B_BYTES + ks * 32, 16, 1024);
-                                        umma_f16(d, ad, bd, idesc, h);
+                                        for (int h = 0; h < 2; ++h) {
+                                            const int ks = cc * 2 + h;
+                                            if (h == 1 && c * 32 + 16 >= p.K) break;  // K16 step past the end adds nothing
+                                            umma_f16(d0 + cc * Cfg::ACC_COLS, a_st + ks * kAStep, b_st + ks * kBStep,
+                                                     idesc, h);
+                                        }
                                     }
                                 }
                                 umma_commit(&tfull[b]);
