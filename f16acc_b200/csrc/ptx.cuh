@@ -125,7 +125,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tm) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
 }
 // 2-D tiled bulk tensor load global -> shared, completion counted on `bar`.
-// c0 is the innermost coordinate (elements).  No cluster multicast.
+// c0 is the innermost coordinate (elements).  One destination CTA: this one.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, uint64_t* bar, int c0, int c1) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::

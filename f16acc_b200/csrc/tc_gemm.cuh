@@ -32,7 +32,7 @@
 //   last warp   store warp: writes each staged tile out (TMA bulk tensor
 //               stores, or plain stores to a strided C and to the peers) and
 //               makes the in-kernel redo decisions.
-// No cluster multicast anywhere; every load reads this GPU's own memory.
+// Every TMA load fills this CTA's own shared memory from this GPU's own memory.
 #pragma once
 
 #include "common.cuh"
