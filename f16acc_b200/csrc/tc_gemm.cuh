@@ -466,12 +466,12 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
         // warp plus every epilogue warp.  FP32 kernel: one thread, mbarriers only.
         // Hang freedom of the bar.sync: (1) each named barrier has one waiter,
         // warp 1 + b, which issues into pair b again only after the round
-        // completes; (2) it checks the abort flag (warp-uniformly) before issuing
-        // and before and after every bar.sync; (3) an epilogue warp that leaves
-        // early raises the flag and then arrives once for each hand-off issued
-        // and not yet released by it (at most one per pair, found issued by its
-        // tfull completing), so the round a waiter is in always fills, and never
-        // overfills.
+        // completes; (2) it checks the abort flag (warp-uniformly) before every
+        // bar.sync and stops there once it is set; (3) an epilogue warp that
+        // leaves early raises the flag and then arrives once for each hand-off
+        // issued and not yet released by it (at most one per pair, found issued
+        // by its tfull completing), so the round a waiter is in always fills,
+        // and never overfills.
         constexpr int NB = 32 * (1 + Cfg::EPI_WARPS);  // release-barrier threads
         if (warp <= ISSUERS && (CHUNKED || lane == 0)) {
             const uint32_t mine = uint32_t(warp - 1);  // chunked: the pair this warp issues into
@@ -498,13 +498,17 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
             auto aborted = [&]() -> bool { return __any_sync(0xffffffffu, *abort_flag != 0); };
             // Before issuing into pair `mine` (chunked): wait until every epilogue
             // warp has loaded the hand-off issued into it before.  False when the
-            // kernel is aborting.
+            // kernel is aborting.  The flag is checked before the bar.sync only:
+            // the instructions between the barrier's release and the next MMAs are
+            // the kernel's critical path (a check there cost 5 % at 4096^3).  A
+            // hand-off issued after a round that an abort completed is harmless:
+            // every epilogue warp has arrived, so none still reads the pair, and
+            // the warp stops at its next check, before any further bar.sync.
             auto reclaim = [&]() -> bool {
                 if (aborted()) return false;
                 if (pending) {
                     named_bar_sync(kPairBarrier + int(mine), NB);
                     pending = false;
-                    if (aborted()) return false;
                 }
                 return true;
             };
@@ -564,12 +568,15 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
                     for (int kb = 0; kb < nkb; ++kb) {
                         if (b == mine) {
                             if (!wait(&full[s], ph)) goto mma_done;
+                            // operands and accumulators of this hand-off, worked out before
+                            // the pair is reclaimed
+                            const uint64_t a_st = a_desc0 + s * kAStage, b_st = b_desc0 + s * kBStage;
+                            const uint32_t d0 = tmem + (2 * b) * Cfg::ACC_COLS;
+                            const bool whole_stage = (kb + 1) * BK <= p.K;
                             if (!reclaim()) goto mma_done;
                             tc_fence_after();
                             if (issue) {
-                                const uint64_t a_st = a_desc0 + s * kAStage, b_st = b_desc0 + s * kBStage;
-                                const uint32_t d0 = tmem + (2 * b) * Cfg::ACC_COLS;
-                                if ((kb + 1) * BK <= p.K) {
+                                if (whole_stage) {
                                     // a whole stage: chunk 2kb into buffer 2b, chunk 2kb+1 into 2b+1
                                     umma_f16(d0, a_st, b_st, idesc, 0u);
                                     umma_f16(d0, a_st + kAStep, b_st + kBStep, idesc, 1u);

@@ -10,7 +10,9 @@ f16acc_b200/csrc/tc_epilogue.cuh, PairRing):
   one `bar.arrive` on named barrier b;
 * before issuing into pair b again, MMA warp b `bar.sync`s on that barrier (a
   round = the MMA warp + every epilogue warp), checking the abort flag before
-  and after; at a normal end it reclaims its last hand-off;
+  the `bar.sync` only (it issues right after the round completes, even when an
+  abort completed it, and stops at its next check); at a normal end it
+  reclaims its last hand-off;
 * an epilogue warp that leaves early raises the abort flag and arrives once
   for the next hand-off of each pair if that hand-off was issued (its tfull
   completes within a bound).
@@ -93,9 +95,6 @@ def run_protocol(seed, n_pairs, n_epi, fail_epi_at=None, fail_mma_at=None, third
                 while bars[w].round == r:
                     yield "blocked"
                 pending = False
-                if state["abort"]:
-                    done = True
-                    break
             state["issued"].add(n)
             pending = True
             n += 2
