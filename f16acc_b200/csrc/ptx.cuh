@@ -311,6 +311,18 @@ __device__ __forceinline__ void add_f16x2_to_f32(float& a0, float& a1, uint32_t 
         : "r"(packed));
 }
 
+// The first chunk of a tile: acc = (float)h + 0 for both halves, the value of
+// the mixed add into a zeroed accumulator (signed zeros included) without the
+// zeroing.
+__device__ __forceinline__ void init_f16x2_to_f32(float& a0, float& a1, uint32_t packed) {
+    asm("{\n\t.reg .f16 lo, hi;\n\t"
+        "mov.b32 {lo, hi}, %2;\n\t"
+        "add.rn.f32.f16 %0, lo, 0f00000000;\n\t"
+        "add.rn.f32.f16 %1, hi, 0f00000000;\n\t}"
+        : "=f"(a0), "=f"(a1)
+        : "r"(packed));
+}
+
 // Non-finite test used for the tile flag: fma(x, 0, s) stays 0 for finite x
 // and turns NaN for +-inf and NaN, so one NaN check at the end of a tile
 // covers every element (|x| < inf is false exactly when x is inf or NaN).

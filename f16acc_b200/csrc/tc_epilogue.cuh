@@ -36,6 +36,11 @@ __device__ __forceinline__ void add_chunk(float (&acc)[CW], const uint32_t (&r)[
 #pragma unroll
     for (int i = 0; i < CW / 2; ++i) add_f16x2_to_f32(acc[2 * i], acc[2 * i + 1], r[i]);
 }
+template <int CW>
+__device__ __forceinline__ void init_chunk(float (&acc)[CW], const uint32_t (&r)[CW / 2]) {
+#pragma unroll
+    for (int i = 0; i < CW / 2; ++i) init_f16x2_to_f32(acc[2 * i], acc[2 * i + 1], r[i]);
+}
 
 // Ring of NBUF accumulators in TMEM shared with the MMA warp (FP32 mode):
 // tfull[b] completes when buffer b's MMAs are done, tempty[b] gets one arrival
@@ -117,8 +122,10 @@ struct PairRing {
     }
 };
 
-// Sum `nchunks` chunks, delivered in pairs, into acc (FP32).  The last pair of
-// a tile holds one chunk when nchunks is odd.  Returns false when a wait gave
+// Sum `nchunks` (>= 1) chunks, delivered in pairs, into acc (FP32); the first
+// chunk initialises acc (the value an add into zeros gives), so acc needs no
+// zeroing at the start of a tile.  The last pair of a tile holds one chunk
+// when nchunks is odd.  Returns false when a wait gave
 // up (no TMEM load is left in flight then).
 template <int CW>
 __device__ __forceinline__ bool consume_chunk_pairs(float (&acc)[CW], int nchunks, PairRing<CW>& ring,
@@ -135,7 +142,10 @@ __device__ __forceinline__ bool consume_chunk_pairs(float (&acc)[CW], int nchunk
         reg_fence(r0);
         if (two) reg_fence(r1);
         ring.release();
-        add_chunk<CW>(acc, r0);
+        if (c == 0)
+            init_chunk<CW>(acc, r0);
+        else
+            add_chunk<CW>(acc, r0);
         if (two) add_chunk<CW>(acc, r1);
     }
     return true;

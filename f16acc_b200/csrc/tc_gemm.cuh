@@ -673,8 +673,6 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
             bool bad = false;
             if constexpr (CHUNKED) {
                 if (main_item) {
-#pragma unroll
-                    for (int j = 0; j < CW; ++j) acc[j] = 0.0f;
                     if (!consume_chunk_pairs<CW>(acc, nchunks, pairs, abort_flag, p.status)) break;
                     // eight independent probe chains (a 64-long chain costs ~300 cycles of
                     // latency at every tile end); NaN in any of them marks the tile
