@@ -269,7 +269,12 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
     TcParams p;
     std::memset(&p, 0, sizeof(p));
     const bool b_mn = !L.b_tma_k;
-    const TcShape shape = tc_shape(chunked != 0);
+    // FP32 mode into a 2-byte C with at least 256 columns: 128x256 tiles, twice
+    // the tensor work per MMA instruction and per stage hand-over (the FP32
+    // kernel is bound by its issuing thread's per-stage path).  Flags and redo
+    // stay on 128x128 tiles.
+    const bool wide = !chunked && c_dtype != F16ACC_OUT_F32 && N >= 256;
+    const TcShape shape = wide ? TcShape{256, 4} : tc_shape(chunked != 0);
     if (v == F16ACC_VARIANT_TCGEN05) {
         const int bn = shape.bn;
         const bool maps_ok =

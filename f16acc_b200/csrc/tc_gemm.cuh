@@ -10,10 +10,12 @@
 //   f16acc/kernel.py:70-71  tile flag = any accumulator not finite.
 //   f16acc/kernel.py:75-81  redo: flagged tiles recomputed in FP32 mode.
 //
-// Design (128 x BN output tiles, 1-CTA UMMA, one CTA per SM at a time):
+// Design (128 x BN output tiles, 1-CTA UMMA, one CTA per SM at a time; BN =
+// 128, or 256 for FP32 mode into a 2-byte C):
 //   warp 0      tile scheduler and TMA producer: A [128 x 64] and B [BN x 64]
 //               (or [64 x BN] when B is N-contiguous) per stage into a 4-stage
-//               smem ring, 128-byte swizzle, completion counted on full[s].
+//               (BN = 256: 3-stage) smem ring, 128-byte swizzle, completion
+//               counted on full[s].
 //   warps 1-2   MMA warps (lane 0 issues; warp 1 owns TMEM).  Chunked mode:
 //               per 64-wide stage, the two 32-long chunks go to the two chunk
 //               buffers of a TMEM pair as two K=16 tcgen05.mma kind::f16 each
@@ -121,7 +123,7 @@ struct TcConfig {
     // of a pair), one in the FP32 kernels, whose single accumulator takes every
     // MMA in order.  Store warps copy staged tiles out to C (and peers): one in
     // the chunked kernel (a tile's copy-out is a few hundred store instructions
-    // against ~40 us of compute), two in the FP32 kernels (a tile every ~25 us).
+    // against ~40 us of compute), two in the FP32 kernels (a tile every ~20 us).
     // Either way 16 epilogue warps make 20 warps, 96 registers a thread (a 21st
     // warp would cut it to 80); 8 make 12 warps and 168.
     static constexpr int MMA_WARPS = CHUNKED_ ? 2 : 1;
@@ -137,11 +139,12 @@ struct TcConfig {
     // whole, coalesced 16-byte-per-lane stores (local C and every peer).  Row
     // pitch padded by 16 bytes so the per-thread row writes spread over banks.
     // Two staging tiles let the epilogue stage tile k+1 while the store warps
-    // copy tile k out; an fp32 tile is twice the size and gets one.
+    // copy tile k out; an fp32 tile is twice the size and gets one, and so does
+    // a 128x256 tile, whose 48 KB stages leave room for three in the ring.
     static constexpr int STAGE_PITCH = BN * OUT_BYTES + 16;
     static constexpr int STAGING_BYTES = BM * STAGE_PITCH;
-    static constexpr int SBUF = OUT_BYTES == 4 ? 1 : 2;
-    static constexpr int STAGES = 4;  // measured: a fifth stage adds nothing to either mode
+    static constexpr int SBUF = (OUT_BYTES == 4 || BN == 256) ? 1 : 2;
+    static constexpr int STAGES = BN == 256 ? 3 : 4;  // measured at BN = 128: a fifth stage adds about 1 %
     static constexpr int TMEM_COLS = 512;
     static constexpr int ACC_COLS = BN;  // one 32-bit TMEM column per accumulator element, f16 or f32
     static constexpr int NBUF = TMEM_COLS / ACC_COLS;
@@ -154,6 +157,8 @@ struct TcConfig {
                   "flag slot split over the epilogue warps");
     static_assert(CW == 32 || CW % 64 == 0, "epilogue column slice");
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
+    // Chunked mode keeps 4 FP16 chunk buffers of BN 32-bit TMEM columns.
+    static_assert(BN == 128 || (BN == 256 && !CHUNKED_), "tile width");
 };
 
 // Write this thread's CW accumulators of one tile row into the smem staging tile.

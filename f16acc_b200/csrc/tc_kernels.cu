@@ -60,12 +60,28 @@ cudaError_t launch_shape(const TcParams& p, bool chunked, bool b_mn, int out, bo
     return cudaErrorInvalidValue;
 }
 
+// 128x256 tiles: FP32 mode (no flags, no redo) with a 2-byte C only.
+cudaError_t launch_wide_fp32(const TcParams& p, bool b_mn, int out, int grid, cudaStream_t stream) {
+    if (b_mn) {
+        if (out == kOutF16) return launch_one<256, 4, false, true, kOutF16, false>(p, grid, stream);
+        if (out == kOutBF16) return launch_one<256, 4, false, true, kOutBF16, false>(p, grid, stream);
+    } else {
+        if (out == kOutF16) return launch_one<256, 4, false, false, kOutF16, false>(p, grid, stream);
+        if (out == kOutBF16) return launch_one<256, 4, false, false, kOutBF16, false>(p, grid, stream);
+    }
+    return cudaErrorInvalidValue;
+}
+
 }  // namespace
 
 bool tc_shape_supported(TcShape s) { return s.bn == 128 && (s.epi_split == 2 || s.epi_split == 4); }
 
 cudaError_t launch_tc(const TcParams& p, TcShape shape, bool chunked, bool b_mn, int out, bool redo, int grid,
                       cudaStream_t stream) {
+    if (shape.bn == 256) {
+        if (chunked || redo || shape.epi_split != 4) return cudaErrorInvalidValue;
+        return launch_wide_fp32(p, b_mn, out, grid, stream);
+    }
     if (shape.bn == 128 && shape.epi_split == 2)
         return launch_shape<128, 2>(p, chunked, b_mn, out, redo, grid, stream);
     if (shape.bn == 128 && shape.epi_split == 4)
