@@ -327,6 +327,11 @@ def run_ours(args):
     mma_sync_tflops = time_torch(
         lambda i: mm_ex(*sets[i % INPUT_SETS], torch.float16, True, variant=_lib.VARIANT_MMA_SYNC,
                         out=outs[i % INPUT_SETS], workspace=wss[i % INPUT_SETS]), reps=GEMMS_PER_STEP)
+    # this library's FP32-accumulate mode (chunked=False: one FP32 accumulator over
+    # all of K, the reference's kernel.py:50-51) on the same products
+    fp32_mode_tflops = time_torch(
+        lambda i: mm_ex(*sets[i % INPUT_SETS], torch.float16, False, out=outs[i % INPUT_SETS]),
+        reps=GEMMS_PER_STEP)
 
     # ---- e2e through the public API with host buffers (pinned), copies inside the timed region.
     # Three streams: uploads of product i+1 and the download of product i-1 overlap product
@@ -410,7 +415,7 @@ def run_ours(args):
             "clocks": clocks.summary(),
             "nshard": nshard,
             "context": {"cublas_f32acc_tflops": cublas_f32, "cublas_f16acc_tflops": cublas_f16,
-                        "mma_sync_tflops": mma_sync_tflops,
+                        "mma_sync_tflops": mma_sync_tflops, "fp32_mode_tflops": fp32_mode_tflops,
                         "reference_published": "65.7 TFLOPS f16acc at 4096^3 on RTX 4060 Ti (README.md:29)"},
         }
     if world > 1:
