@@ -149,10 +149,12 @@ int f16acc_gemm_allgather(const void *A, int64_t sAm, int64_t sAk,
                           int64_t M, int64_t N, int64_t K, int chunked,
                           void *workspace, size_t ws_bytes, int device, void *stream);
 
-/* What f16acc_gemm_ex would run for these operands, without launching:
- * variant (F16ACC_VARIANT_TCGEN05 or _MMA_SYNC), output tile shape, and the
- * tile grid (flag slot of tile (tm, tn) = tm * tiles_n + tn, each slot
- * f16acc_flag_bytes_per_tile() bytes, non-zero bytes = flagged). */
+/* What f16acc_gemm_ex would run for these operands in chunked mode, without
+ * launching: variant (F16ACC_VARIANT_TCGEN05 or _MMA_SYNC), output tile shape,
+ * and the tile grid of the flags (flag slot of tile (tm, tn) = tm * tiles_n +
+ * tn, each slot f16acc_flag_bytes_per_tile() bytes, non-zero bytes =
+ * flagged).  A chunked == 0 call on the tcgen05 variant into a 2-byte C with
+ * N >= 256 runs on 128x256 tiles; it writes no flags. */
 typedef struct f16acc_plan {
     int variant;
     int tile_m, tile_n;
@@ -166,7 +168,9 @@ int f16acc_flag_bytes_per_tile(void);
 /* tcgen05 tile configuration for later calls, process-wide: output columns
  * per tile (128) and epilogue column slices per TMEM lane quarter (2 or 4,
  * i.e. 8 or 16 epilogue warps; 0 = the default, 2 for chunked accumulation
- * and 4 for FP32 accumulation).  A tuning knob; results do not depend on it. */
+ * and 4 for FP32 accumulation).  It does not apply to the 128x256 tiles of
+ * chunked == 0 calls into a 2-byte C.  A tuning knob; results do not depend
+ * on it. */
 int f16acc_set_tc_config(int tile_n, int epi_split);
 
 /* Cap the SMs a GEMM launch occupies, process-wide, for later calls (0 = all
