@@ -47,6 +47,8 @@ INPUT_SETS = 4
 METRIC = "TFLOPS @4096^3 FP16 (chunked FP16-accumulate GEMM, f16acc.mm)"
 UNIT = "TFLOPS"
 FALLBACK_PEAK_TFLOPS = 1590.0
+# Where the JSON result line goes (the real stdout; see __main__).
+RESULT_OUT = sys.stdout
 
 
 def flops_per_gemm() -> float:
@@ -217,7 +219,7 @@ def run_reference(args):
                          "torch_threads": __import__("torch").get_num_threads()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    print(json.dumps(line), file=RESULT_OUT, flush=True)
     return 0
 
 
@@ -424,7 +426,7 @@ def run_ours(args):
         dist.barrier()
         dist.destroy_process_group()
     if line is not None:
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=RESULT_OUT, flush=True)
     return 0
 
 
@@ -627,7 +629,7 @@ def run_workload(args):
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=RESULT_OUT, flush=True)
     return 0
 
 
@@ -659,4 +661,10 @@ def main(argv=None):
 
 
 if __name__ == "__main__":
+    # The result is one JSON line on stdout.  Anything else a library writes to
+    # the process's stdout (NCCL prints its version banner there when its
+    # debug output is on) is sent to stderr instead.
+    sys.stdout.flush()
+    RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     sys.exit(main())
