@@ -203,6 +203,18 @@ int f16acc_set_redo_mode(int mode);
 #define F16ACC_SCHEDULE_DYNAMIC 1
 int f16acc_set_schedule(int mode);
 
+/* Tile width of FP32-mode calls (chunked == 0) into a 2-byte C, process-wide,
+ * for later calls: F16ACC_FP32_TILES_AUTO (the default) takes 128x256 tiles
+ * when N >= 256 and they finish in fewer modelled tile-times than 128x128
+ * ones (a wide tile costs about 1.5 narrow ones), F16ACC_FP32_TILES_WIDE takes
+ * them whenever N >= 256, F16ACC_FP32_TILES_NARROW never.  Every output
+ * element gets the same K16 MMA sequence either way, so results are
+ * bit-identical.  Returns the previous setting. */
+#define F16ACC_FP32_TILES_AUTO 0
+#define F16ACC_FP32_TILES_WIDE 1
+#define F16ACC_FP32_TILES_NARROW 2
+int f16acc_set_fp32_tiles(int mode);
+
 /* Raw-rate probes, the B200 counterparts of the reference's bench/rate.py and
  * bench/chunkrate.py (measurement aids).  tcgen05 modes: `grid` CTAs (one per
  * SM) each run `chunks` 32-long chunks of 128x128 MMAs on a fixed

@@ -71,3 +71,12 @@ def test_plan_without_a_gpu_is_mma_sync_or_tcgen05():
     rc = _lib.load().f16acc_get_plan(16, 64, 1, 16, 1, 64, 128, 128, 64, _lib.VARIANT_MMA_SYNC, p)
     assert rc == _lib.OK and p.variant == _lib.VARIANT_MMA_SYNC and (p.tile_m, p.tile_n) == (128, 128)
     assert (p.tiles_m, p.tiles_n) == (1, 1)
+
+
+def test_tuning_knobs_validate_and_return_the_previous_setting():
+    lib = _lib.load()
+    assert lib.f16acc_set_fp32_tiles(7) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.f16acc_set_fp32_tiles(_lib.FP32_TILES_WIDE) == _lib.FP32_TILES_AUTO
+    assert lib.f16acc_set_fp32_tiles(_lib.FP32_TILES_AUTO) == _lib.FP32_TILES_WIDE
+    assert lib.f16acc_set_schedule(5) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.f16acc_set_redo_mode(5) == _lib.ERR_INVALID_ARGUMENT

@@ -1,10 +1,12 @@
-"""FP32 mode (`chunked=False`) into a 2-byte C with N >= 256 runs on 128x256
-tiles; every other FP32-mode call (fp32 C, N < 256, the redo of flagged tiles)
-runs on 128x128 tiles.  Both issue the same K16 MMA sequence per output
-element, so a wide-tile result must equal the 128-wide FP32 result rounded to
-the output type, bit for bit (f16acc/kernel.py:50-51: one FP32 accumulator
-over all of K, then the cast), and stay within FP32 accumulation error of an
-FP64 product."""
+"""FP32 mode (`chunked=False`) into a 2-byte C with N >= 256 may run on
+128x256 tiles (f16acc_set_fp32_tiles: by a wave model, always, or never);
+every other FP32-mode call (fp32 C, N < 256, the redo of flagged tiles) runs on
+128x128 tiles.  Both issue the same K16 MMA sequence per output element, so
+the results must be identical bit for bit (f16acc/kernel.py:50-51: one FP32
+accumulator over all of K, then the cast), and within FP32 accumulation error
+of an FP64 product."""
+
+from contextlib import contextmanager
 
 import pytest
 import torch
@@ -13,6 +15,17 @@ from f16acc_b200 import _lib
 from f16acc_b200.kernel import mm, mm_ex, plan, tile_flags
 
 pytestmark = pytest.mark.gpu
+
+
+@contextmanager
+def fp32_tiles(mode):
+    lib = _lib.load()
+    prev = lib.f16acc_set_fp32_tiles(mode)
+    assert prev >= 0
+    try:
+        yield
+    finally:
+        lib.f16acc_set_fp32_tiles(prev)
 
 F32_TOL = 1e-5  # FP32 accumulation vs FP64, of max|ref|
 
@@ -42,9 +55,14 @@ def operands(M, N, K, layout, cuda, seed):
 def test_wide_tiles_equal_the_128_wide_fp32_path(cuda, M, N, K, layout, out_dtype):
     a, b = operands(M, N, K, layout, cuda, seed=M + N + K)
     assert plan(a, b)["variant"] == _lib.VARIANT_TCGEN05  # strides TMA can take
-    wide = mm(a, b, out_dtype, chunked=False)      # 128x256 tiles
+    with fp32_tiles(_lib.FP32_TILES_WIDE):
+        wide = mm(a, b, out_dtype, chunked=False)
+    with fp32_tiles(_lib.FP32_TILES_NARROW):
+        narrow_same_type = mm(a, b, out_dtype, chunked=False)
     narrow = mm(a, b, torch.float32, chunked=False)  # 128x128 tiles, fp32 C
+    assert torch.equal(wide, narrow_same_type)
     assert torch.equal(wide, narrow.to(out_dtype))
+    assert torch.equal(mm(a, b, out_dtype, chunked=False), wide)  # the default choice, whichever it is
     ref = a.double() @ b.double()
     err = (narrow.double() - ref).abs().max().item()
     assert err <= ref.abs().max().item() * F32_TOL
@@ -56,7 +74,8 @@ def test_wide_tiles_strided_output(cuda):
     M, N, K = 384, 768, 320
     a, b = operands(M, N, K, "w_t", cuda, seed=9)
     out = torch.empty(N, M, device=cuda, dtype=torch.float16).t()
-    c, _ = mm_ex(a, b, torch.float16, chunked=False, out=out)
+    with fp32_tiles(_lib.FP32_TILES_WIDE):
+        c, _ = mm_ex(a, b, torch.float16, chunked=False, out=out)
     assert c.data_ptr() == out.data_ptr()
     narrow = mm(a, b, torch.float32, chunked=False)
     assert torch.equal(c, narrow.half())
@@ -78,5 +97,7 @@ def test_wide_tiles_match_redone_tiles(cuda):
     assert flags.any()
     tm, tn = plan(a, b)["tile"]
     mask = flags.repeat_interleave(tm, 0).repeat_interleave(tn, 1)[:n, :n]
-    c32 = mm(a, b, torch.float16, chunked=False)
+    with fp32_tiles(_lib.FP32_TILES_WIDE):
+        c32 = mm(a, b, torch.float16, chunked=False)
     assert torch.equal(c[mask], c32[mask])
+
