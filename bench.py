@@ -518,11 +518,25 @@ def one_product(args, dev):
         times.append((e0, e1))
     torch.cuda.synchronize()
     med = statistics.median(e0.elapsed_time(e1) for e0, e1 in times)
+    # Host cost of one call of the public `mm` (checks, output and workspace
+    # allocation from the caching allocator, the C call and its launch), with
+    # the GPU kept busy behind a device sleep so the calls only enqueue.
+    from f16acc_b200.kernel import mm
+
+    host_us = None
+    if args.host_calls > 0:
+        torch.cuda._sleep(200_000_000)
+        t0 = time.perf_counter()
+        for _ in range(args.host_calls):
+            mm(a, b, out_dtype, chunked)
+        host_us = (time.perf_counter() - t0) / args.host_calls * 1e6
+        torch.cuda.synchronize()
     ref = a.double() @ b.double()
     return {"config": f"one product {m}x{n}x{k}, {args.layout} B, {args.out_dtype} out, "
                       f"{'FP32' if args.fp32_acc else 'chunked FP16'} accumulate",
             "kernel": _lib.VARIANT_NAMES[plan(a, b, variant)["variant"]], "median_ms": med,
-            "tflops": 2.0 * m * n * k / (med / 1e3) / 1e12, "max_rel_err_vs_fp64": rel_err(c, ref)}
+            "tflops": 2.0 * m * n * k / (med / 1e3) / 1e12, "max_rel_err_vs_fp64": rel_err(c, ref),
+            "host_us_per_mm_call": host_us}
 
 
 def run_workload(args):
@@ -652,6 +666,8 @@ def main(argv=None):
     ap.add_argument("--out-dtype", choices=["f16", "f32"], default="f16", help="output type, --workload one")
     ap.add_argument("--fp32-acc", action="store_true", help="--workload one: chunked=False (plain FP32 accumulate)")
     ap.add_argument("--reps", type=int, default=10, help="timed products for --workload one")
+    ap.add_argument("--host-calls", type=int, default=0,
+                    help="--workload one: also time the host side of this many mm() calls (enqueue only)")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)

@@ -18,11 +18,27 @@ function of the operands, so `mm` may be called from several threads.
 
 from __future__ import annotations
 
+import functools
+
 import torch
 
 from . import _lib
 
 _OUT_CODES = {torch.float16: _lib.OUT_F16, torch.float32: _lib.OUT_F32, torch.bfloat16: _lib.OUT_BF16}
+
+# The current stream's raw handle for a device index: torch's own accessor
+# (the one its generated kernels launch through) when present, which costs a
+# fraction of building a torch.cuda.Stream object per call.
+if hasattr(torch._C, "_cuda_getCurrentRawStream"):
+    _raw_stream = torch._C._cuda_getCurrentRawStream
+else:  # pragma: no cover - older torch
+    def _raw_stream(index):
+        return torch.cuda.current_stream(index).cuda_stream
+
+
+def _device_index(t) -> int:
+    index = t.device.index
+    return index if index is not None else torch.cuda.current_device()
 
 
 def _check(a, b):
@@ -41,6 +57,7 @@ def _raise(rc: int):
     raise RuntimeError(f"f16acc_b200: {msg} (code {rc})")
 
 
+@functools.lru_cache(maxsize=4096)
 def workspace_bytes(M: int, N: int, K: int) -> int:
     return int(_lib.load().f16acc_workspace_bytes(M, N, K))
 
@@ -73,14 +90,14 @@ def mm_ex(a, b, out_dtype=torch.float16, chunked=True, *, variant=_lib.VARIANT_A
         raise ValueError("out must be an (M, N) tensor of out_dtype on the operands' device")
     ws_ptr, ws_len = None, 0
     if chunked:
-        need = int(lib.f16acc_workspace_bytes(M, N, K))
+        need = workspace_bytes(M, N, K)
         if workspace is None:
             workspace = torch.empty(need, dtype=torch.uint8, device=a.device)
         elif workspace.numel() < need or workspace.device != a.device or workspace.dtype != torch.uint8:
             raise ValueError(f"workspace must be a uint8 tensor of at least {need} bytes on the operands' device")
         ws_ptr, ws_len = workspace.data_ptr(), workspace.numel()
-    dev = a.device.index if a.device.index is not None else torch.cuda.current_device()
-    stream = torch.cuda.current_stream(a.device).cuda_stream
+    dev = _device_index(a)
+    stream = _raw_stream(dev)
     if bias is None:
         rc = lib.f16acc_gemm_ex(a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(), b.stride(0), b.stride(1),
                                 out.data_ptr(), out.stride(0), out.stride(1), code, M, N, K, 1 if chunked else 0,
@@ -121,12 +138,12 @@ def mm(a, b, out_dtype=torch.float16, chunked=True):
     c = torch.empty(M, N, device=a.device, dtype=out_dtype)
     ws_ptr, ws_len, ws = None, 0, None
     if chunked:
-        ws = torch.empty(int(lib.f16acc_workspace_bytes(M, N, K)), dtype=torch.uint8, device=a.device)
+        ws = torch.empty(workspace_bytes(M, N, K), dtype=torch.uint8, device=a.device)
         ws_ptr, ws_len = ws.data_ptr(), ws.numel()
-    dev = a.device.index if a.device.index is not None else torch.cuda.current_device()
+    dev = _device_index(a)
     rc = lib.f16acc_gemm(a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(), b.stride(0), b.stride(1),
                          c.data_ptr(), c.stride(0), c.stride(1), code, M, N, K, 1 if chunked else 0,
-                         ws_ptr, ws_len, dev, torch.cuda.current_stream(a.device).cuda_stream)
+                         ws_ptr, ws_len, dev, _raw_stream(dev))
     if rc != _lib.OK:
         _raise(rc)
     return c
@@ -144,11 +161,11 @@ def mm_phase(phase, a, b, out, workspace, chunked=True, variant=_lib.VARIANT_AUT
     fn = {"main": lib.f16acc_gemm_main, "redo": lib.f16acc_gemm_redo}[phase]
     M, K = a.shape
     N = b.shape[1]
-    dev = a.device.index if a.device.index is not None else torch.cuda.current_device()
+    dev = _device_index(a)
     ws_ptr, ws_len = (workspace.data_ptr(), workspace.numel()) if workspace is not None else (None, 0)
     rc = fn(a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(), b.stride(0), b.stride(1),
             out.data_ptr(), out.stride(0), out.stride(1), code, M, N, K, 1 if chunked else 0,
-            ws_ptr, ws_len, dev, torch.cuda.current_stream(a.device).cuda_stream, int(variant))
+            ws_ptr, ws_len, dev, _raw_stream(dev), int(variant))
     if rc != _lib.OK:
         _raise(rc)
 
