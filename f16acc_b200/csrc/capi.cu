@@ -161,20 +161,27 @@ std::atomic<int> g_schedule{F16ACC_SCHEDULE_DYNAMIC};
 std::atomic<int> g_fp32_tiles{F16ACC_FP32_TILES_AUTO};
 constexpr int kGroupM = 8;
 
-// Rows up to which the few-row kernel is the automatic choice.
+// Rows up to which the few-row kernel is the automatic choice: 64, except
+// for very wide products (lm_head-sized N), where at 64 rows the tcgen05
+// kernel is faster (measured on the 1536 x 151936 weight: 110 against 148 us);
+// there the few-row kernel is chosen up to 32 rows.
 constexpr int64_t kSkinnyMaxRows = 64;
+constexpr int64_t kSkinnyMaxRowsWide = 32;
+constexpr int64_t kSkinnyWideN = 32768;
 
 int choose_variant(const Layout& L, int64_t M, int64_t N, int64_t K, int requested, bool peers = false) {
     const bool dims_ok = M < (int64_t(1) << 31) && N < (int64_t(1) << 31) && K < (int64_t(1) << 31);
     const bool tc_ok = dims_ok && K > 0 && L.a_tma && (L.b_tma_k || L.b_tma_n) && encode_fn() != nullptr;
     // cp.async wants 16-byte aligned rows with unit inner stride; no peer stores
     const bool skinny_ok = dims_ok && K > 0 && M <= kSkinnyMaxRows && L.a_vec && (L.b_kvec || L.b_nvec) && !peers;
+    const bool skinny_auto = skinny_ok && (M <= kSkinnyMaxRowsWide || N <= kSkinnyWideN);
     if (requested == F16ACC_VARIANT_TCGEN05) return tc_ok ? F16ACC_VARIANT_TCGEN05 : -1;
     if (requested == F16ACC_VARIANT_MMA_SYNC) return dims_ok ? F16ACC_VARIANT_MMA_SYNC : -1;
     if (requested == F16ACC_VARIANT_SKINNY) return skinny_ok ? F16ACC_VARIANT_SKINNY : -1;
     if (requested != F16ACC_VARIANT_AUTO) return -1;
-    if (skinny_ok) return F16ACC_VARIANT_SKINNY;
+    if (skinny_auto) return F16ACC_VARIANT_SKINNY;
     if (tc_ok) return F16ACC_VARIANT_TCGEN05;
+    if (skinny_ok) return F16ACC_VARIANT_SKINNY;
     return dims_ok ? F16ACC_VARIANT_MMA_SYNC : -1;
 }
 

@@ -56,15 +56,20 @@ struct SkinnyCfg {
     static constexpr int MAX_S = 8;      // portable cluster size
     static constexpr int TARGET_CTAS = 296;  // the split aims at one wave of two CTAs per SM of a B200
     // Ring depth: as many stages as keep two CTAs resident per SM (the bytes in
-    // flight per SM are what the streaming of B needs).
-    template <int MT>
-    static constexpr int stages() { return MT == 1 ? 5 : 4; }
+    // flight per SM are what the streaming of B needs).  SHALLOW, for launches
+    // of more single-CTA tiles than one wave holds (lm_head-sized N): 3 stages,
+    // so three CTAs fit per SM and one's pipeline fill and tile end overlap the
+    // others' streaming (measured on the lm_head shape at M = 1 / 16 / 32:
+    // 96.6 -> 88.5, 100.8 -> 94.7, 117 -> 104 us; with a K split, or at 64
+    // rows, the deeper ring is faster).
+    template <int MT, bool SHALLOW = false>
+    static constexpr int stages() { return SHALLOW ? 3 : (MT == 1 ? 5 : 4); }
     template <int MT>
     static constexpr int a_elems() { return 16 * MT * LDK; }
     template <bool B_KN>
     static constexpr int b_elems() { return B_KN ? BK * LDN : BN * LDK; }
-    template <int MT, bool B_KN>
-    static constexpr int smem_bytes() { return stages<MT>() * (a_elems<MT>() + b_elems<B_KN>()) * 2; }
+    template <int MT, bool B_KN, bool SHALLOW = false>
+    static constexpr int smem_bytes() { return stages<MT, SHALLOW>() * (a_elems<MT>() + b_elems<B_KN>()) * 2; }
     static constexpr int RED_LD = BN + 4;  // FP32 partial tile pitch (floats)
 };
 
@@ -82,11 +87,11 @@ __device__ __forceinline__ void cp_async_wait() {
 // Sum this CTA's K range [k_begin, k_end) into acc (FP32): chunk by chunk in FP16
 // (CHUNKED) or straight FP32 accumulation.  Leaves every cp.async drained and
 // the ring free (it ends with a __syncthreads).
-template <int MT, bool CHUNKED, bool B_KN>
+template <int MT, bool CHUNKED, bool B_KN, bool SHALLOW>
 __device__ __forceinline__ void skinny_mainloop(const SkinnyParams& p, __half* sA, __half* sB, int n0, int k_begin,
                                                 int k_end, float (&acc)[MT][4][4]) {
     using Cfg = SkinnyCfg;
-    constexpr int BK = Cfg::BK, STAGES = Cfg::stages<MT>(), LDK = Cfg::LDK, LDN = Cfg::LDN;
+    constexpr int BK = Cfg::BK, STAGES = Cfg::stages<MT, SHALLOW>(), LDK = Cfg::LDK, LDN = Cfg::LDN;
     constexpr int A_EL = Cfg::a_elems<MT>(), B_EL = Cfg::b_elems<B_KN>();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 #pragma unroll
@@ -283,14 +288,14 @@ __device__ __forceinline__ bool skinny_reduce_store(cooperative_groups::cluster_
 
 // grid (ceil(N / 128), S), cluster (1, S, 1).  REDO: the separate FP32 pass
 // over flagged tiles (launched behind the chunked pass).
-template <int MT, bool CHUNKED, bool B_KN, int OUT, bool REDO>
+template <int MT, bool CHUNKED, bool B_KN, int OUT, bool REDO, bool SHALLOW>
 __global__ void __launch_bounds__(SkinnyCfg::THREADS) skinny_gemm_kernel(const __grid_constant__ SkinnyParams p) {
     namespace cg = cooperative_groups;
     using Cfg = SkinnyCfg;
     static_assert(!(CHUNKED && REDO), "the redo pass runs in FP32 mode");
     extern __shared__ __align__(128) uint8_t skinny_smem[];
     __half* sA = reinterpret_cast<__half*>(skinny_smem);
-    __half* sB = sA + Cfg::stages<MT>() * Cfg::a_elems<MT>();
+    __half* sB = sA + Cfg::stages<MT, SHALLOW>() * Cfg::a_elems<MT>();
     float* red = reinterpret_cast<float*>(skinny_smem);  // the ring, reused once the main loop is done
     __shared__ int tile_bad;                            // OR over the cluster of "saw a non-finite sum"
 
@@ -311,7 +316,7 @@ __global__ void __launch_bounds__(SkinnyCfg::THREADS) skinny_gemm_kernel(const _
     if (threadIdx.x == 0) tile_bad = 0;  // before the first cluster barrier: peers OR into it after
 
     float acc[MT][4][4];
-    skinny_mainloop<MT, CHUNKED, B_KN>(p, sA, sB, n0, k_begin, k_end, acc);
+    skinny_mainloop<MT, CHUNKED, B_KN, SHALLOW>(p, sA, sB, n0, k_begin, k_end, acc);
     skinny_store_partial<MT>(red, acc);
     cluster.sync();  // every partial tile is in its CTA's shared memory
     const bool bad = skinny_reduce_store<MT, OUT>(cluster, red, S, rank, p, n0);
@@ -326,7 +331,7 @@ __global__ void __launch_bounds__(SkinnyCfg::THREADS) skinny_gemm_kernel(const _
                 make_uint4(tile_bad ? 1u : 0u, 0u, 0u, 0u);
         if (!(p.inline_redo && tile_bad)) return;
         // The flagged tile again in FP32 mode: the FP32 kernel's loop and summation order.
-        skinny_mainloop<MT, false, B_KN>(p, sA, sB, n0, k_begin, k_end, acc);
+        skinny_mainloop<MT, false, B_KN, SHALLOW>(p, sA, sB, n0, k_begin, k_end, acc);
         skinny_store_partial<MT>(red, acc);
         cluster.sync();
         skinny_reduce_store<MT, OUT>(cluster, red, S, rank, p, n0);

@@ -8,10 +8,10 @@
 namespace f16acc {
 namespace {
 
-template <int MT, bool CHUNKED, bool B_KN, int OUT, bool REDO>
+template <int MT, bool CHUNKED, bool B_KN, int OUT, bool REDO, bool SHALLOW>
 cudaError_t launch_one(const SkinnyParams& p, int tiles_n, int splits, cudaStream_t stream) {
-    auto kernel = skinny_gemm_kernel<MT, CHUNKED, B_KN, OUT, REDO>;
-    constexpr int smem = SkinnyCfg::smem_bytes<MT, B_KN>();
+    auto kernel = skinny_gemm_kernel<MT, CHUNKED, B_KN, OUT, REDO, SHALLOW>;
+    constexpr int smem = SkinnyCfg::smem_bytes<MT, B_KN, SHALLOW>();
     cudaError_t e = ensure_smem_attr(kernel, smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
@@ -35,11 +35,21 @@ cudaError_t launch_one(const SkinnyParams& p, int tiles_n, int splits, cudaStrea
     return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
+template <int MT, bool B_KN, int OUT, bool SHALLOW>
+cudaError_t launch_depth(const SkinnyParams& p, bool chunked, bool redo, int tiles_n, int splits, cudaStream_t s) {
+    if (redo) return launch_one<MT, false, B_KN, OUT, true, SHALLOW>(p, tiles_n, splits, s);
+    if (chunked) return launch_one<MT, true, B_KN, OUT, false, SHALLOW>(p, tiles_n, splits, s);
+    return launch_one<MT, false, B_KN, OUT, false, SHALLOW>(p, tiles_n, splits, s);
+}
+
+// The shallow ring for up to 32 rows and more single-CTA tiles than one wave
+// of two CTAs per SM holds (SkinnyCfg::stages; at 64 rows it measured 4.6 %
+// slower on the lm_head shape).
 template <int MT, bool B_KN, int OUT>
 cudaError_t launch_mode(const SkinnyParams& p, bool chunked, bool redo, int tiles_n, int splits, cudaStream_t s) {
-    if (redo) return launch_one<MT, false, B_KN, OUT, true>(p, tiles_n, splits, s);
-    if (chunked) return launch_one<MT, true, B_KN, OUT, false>(p, tiles_n, splits, s);
-    return launch_one<MT, false, B_KN, OUT, false>(p, tiles_n, splits, s);
+    return MT <= 2 && splits == 1 && tiles_n > SkinnyCfg::TARGET_CTAS
+               ? launch_depth<MT, B_KN, OUT, true>(p, chunked, redo, tiles_n, splits, s)
+               : launch_depth<MT, B_KN, OUT, false>(p, chunked, redo, tiles_n, splits, s);
 }
 
 template <int MT, bool B_KN>

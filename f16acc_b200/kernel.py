@@ -6,7 +6,8 @@ signature, the same ValueError checks and messages, C allocated here with
 `out_dtype`, a per-call flag workspace from the caching allocator, and an
 asynchronous launch on the current stream with no host sync.  The work itself
 is the native library (include/f16acc.h): a warp-specialised tcgen05/TMA
-kernel when the operands allow TMA, a few-row kernel for M <= 64, else a
+kernel when the operands allow TMA, a few-row kernel for M <= 64 (M <= 32
+when N > 32768), else a
 warp-level mma.sync kernel that takes any strides.  Tiles whose FP16 chunk
 overflowed are redone with FP32 accumulation on the device: inside the same
 tcgen05 launch by default, otherwise by a second kernel launched behind the

@@ -50,12 +50,13 @@ extern "C" {
 #define F16ACC_OUT_BF16 2
 
 /* Kernel variants for f16acc_gemm_ex (measurement and tests). */
-#define F16ACC_VARIANT_AUTO 0     /* skinny for M <= 64, else tcgen05 when the operands allow TMA, else mma.sync */
+#define F16ACC_VARIANT_AUTO 0     /* skinny for M <= 64 (M <= 32 when N > 32768), else tcgen05 when the operands
+                                     allow TMA, else mma.sync */
 #define F16ACC_VARIANT_TCGEN05 1  /* warp-specialised tcgen05/TMA kernel only */
 #define F16ACC_VARIANT_MMA_SYNC 2 /* warp-level mma.sync kernel (any strides) */
 #define F16ACC_VARIANT_SKINNY 3   /* few rows (M <= 64): mma.sync tiles, K split over a CTA cluster;
                                      K-contiguous A and K- or N-contiguous B with 16-byte aligned rows.
-                                     The automatic choice for M <= 64. */
+                                     The automatic choice for M <= 64 (M <= 32 when N > 32768). */
 
 /*
  * C[M,N] = A[M,K] @ B[K,N].  Replaces kernel.py:84-105 `mm`.

@@ -1,4 +1,4 @@
-"""The few-row kernel (F16ACC_VARIANT_SKINNY, the automatic choice for M <= 64):
+"""The few-row kernel (F16ACC_VARIANT_SKINNY, the automatic choice for M <= 64, M <= 32 when N > 32768):
 parity with the CPU oracle, flags, the redo, bias and layouts.
 
 Its chunk values are the same m16n8k16 FP16-accumulate results as the other
@@ -60,6 +60,9 @@ def test_k_and_n_tails(cuda, K, N):
 def test_automatic_choice(cuda):
     for M, want in ((1, SK), (64, SK), (65, _lib.VARIANT_TCGEN05)):
         a, b = operands(M, 256, 256, seed=1, device=cuda)
+        assert plan(a, b)["variant"] == want
+    for M, want in ((32, SK), (33, _lib.VARIANT_TCGEN05)):  # very wide products
+        a, b = operands(M, 40000, 64, seed=1, device=cuda)
         assert plan(a, b)["variant"] == want
     a, b = operands(16, 256, 256, seed=1, device=cuda)
     assert plan(a[:, 1:], b[1:])["variant"] != SK  # unaligned rows: not a cp.async operand
