@@ -115,6 +115,37 @@ def test_flags_and_redo(cuda, M):
     assert torch.equal(c, c2)
 
 
+@pytest.mark.parametrize("M", [1, 17, 32])
+def test_wide_launch_shallow_ring(cuda, M):
+    # more single-CTA column tiles than one wave holds (N = 38017: 298 tiles,
+    # the last 1 column wide): the 3-stage ring; parity with the oracle, flags
+    # and the in-kernel redo of two overflowing tiles
+    N, K = 38017, 200
+    g = torch.Generator().manual_seed(M)
+    a = torch.randn(M, K, generator=g)
+    w = torch.randn(N, K, generator=g)
+    a[0] *= 300.0
+    w[5] *= 300.0       # tile 0
+    w[38000] *= 300.0   # tile 296
+    a, w = a.half().to(cuda), w.half().to(cuda)
+    b = w.t()
+    assert plan(a, b)["variant"] == SK
+    c, ws = mm_ex(a, b, torch.float32)
+    pl = plan(a, b, SK)
+    flags = tile_flags(ws, pl).cpu().numpy()
+    _, oflags = O.gemm_chunked(np16(a), np16(b), round_every=16, tile=pl["tile"], redo=False)
+    np.testing.assert_array_equal(flags, oflags.astype(bool))
+    assert flags[0, 0] and flags[0, 296] and flags.sum() == 2
+    c32, _ = mm_ex(a, b, torch.float32, chunked=False)
+    tn = pl["tile"][1]
+    mask = np.repeat(flags[0], tn)[:N]
+    assert torch.equal(c[:, torch.from_numpy(mask).to(cuda)], c32[:, torch.from_numpy(mask).to(cuda)])
+    ref, _ = O.gemm_chunked(np16(a), np16(b), round_every=16)
+    bound = chunk_ulp_bound(np16(a), np16(b))
+    err = np.abs(c.double().cpu().numpy() - ref)
+    assert (err[:, ~mask] <= bound[:, ~mask]).all()
+
+
 def test_overflow_known_answer(cuda):
     # tests/test_f16acc.py:91-101 with 16 rows: every chunk overflows, the answer is exactly 100
     x = torch.full((16, 64), 100.0, device=cuda).half()
