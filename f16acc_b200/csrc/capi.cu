@@ -157,7 +157,7 @@ std::atomic<int> g_redo_mode{F16ACC_REDO_INLINE};
 // Tile order of the chunked main pass (F16ACC_SCHEDULE_*).
 std::atomic<int> g_schedule{F16ACC_SCHEDULE_DYNAMIC};
 
-// Tile width of FP32-mode calls into a 2-byte C (F16ACC_FP32_TILES_*).
+// Tile width of FP32-mode calls (F16ACC_FP32_TILES_*).
 std::atomic<int> g_fp32_tiles{F16ACC_FP32_TILES_AUTO};
 constexpr int kGroupM = 8;
 
@@ -279,7 +279,7 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
     TcParams p;
     std::memset(&p, 0, sizeof(p));
     const bool b_mn = !L.b_tma_k;
-    // FP32 mode into a 2-byte C with at least 256 columns: 128x256 tiles, twice
+    // FP32 mode into C with at least 256 columns: 128x256 tiles, twice
     // the tensor work per MMA instruction and per stage hand-over (the FP32
     // kernel is bound by its issuing thread's per-stage path), when they finish
     // sooner: a wide tile takes about 1.52x a 128-wide one (35.7 against 23.4
@@ -289,7 +289,7 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
     const int64_t waves_narrow = cdiv(cdiv(M, 128) * cdiv(N, 128), sms_all);
     const int64_t waves_wide = cdiv(cdiv(M, 128) * cdiv(N, 256), sms_all);
     const int fp32_tiles = g_fp32_tiles.load(std::memory_order_relaxed);
-    const bool wide = !chunked && c_dtype != F16ACC_OUT_F32 && N >= 256 &&
+    const bool wide = !chunked && N >= 256 &&
                       (fp32_tiles == F16ACC_FP32_TILES_WIDE ||
                        (fp32_tiles == F16ACC_FP32_TILES_AUTO && double(waves_wide) * 1.52 < double(waves_narrow)));
     const TcShape shape = wide ? TcShape{256, 4} : tc_shape(chunked != 0);

@@ -11,7 +11,7 @@
 //   f16acc/kernel.py:75-81  redo: flagged tiles recomputed in FP32 mode.
 //
 // Design (128 x BN output tiles, 1-CTA UMMA, one CTA per SM at a time; BN =
-// 128, or 256 for FP32 mode into a 2-byte C):
+// 128, or 256 in FP32 mode):
 //   warp 0      tile scheduler and TMA producer: A [128 x 64] and B [BN x 64]
 //               (or [64 x BN] when B is N-contiguous) per stage into a 4-stage
 //               (BN = 256: 3-stage) smem ring, 128-byte swizzle, completion
@@ -95,7 +95,7 @@ struct alignas(16) TcCtrl {
     uint64_t tfull[NBUF], tempty[NBUF];
     uint64_t sched_full[kSchedDepth], sched_empty[kSchedDepth];
     uint64_t st_full[2], st_empty[2];  // staging tile b: staged by the epilogue / copied out by the store warps
-    int4 st_meta[2];                   // {tm, tn, TcStore kind, 0} of the tile in staging b
+    int4 st_meta[2];                   // {tm, tn, TcStore kind, column half} of the tile in staging b
     uint64_t clc_bar, drain;
     uint32_t tmem_slot;
     int abort_flag;
@@ -140,8 +140,12 @@ struct TcConfig {
     // pitch padded by 16 bytes so the per-thread row writes spread over banks.
     // Two staging tiles let the epilogue stage tile k+1 while the store warps
     // copy tile k out; an fp32 tile is twice the size and gets one, and so does
-    // a 128x256 tile, whose 48 KB stages leave room for three in the ring.
-    static constexpr int STAGE_PITCH = BN * OUT_BYTES + 16;
+    // a 128x256 tile, whose 48 KB stages leave room for three in the ring.  An
+    // fp32 128x256 tile (128 KB) is staged one 128-column half at a time, a
+    // hand-over each.
+    static constexpr int STAGE_COLS = (BN == 256 && OUT_BYTES == 4) ? 128 : BN;
+    static constexpr int HALVES = BN / STAGE_COLS;
+    static constexpr int STAGE_PITCH = STAGE_COLS * OUT_BYTES + 16;
     static constexpr int STAGING_BYTES = BM * STAGE_PITCH;
     static constexpr int SBUF = (OUT_BYTES == 4 || BN == 256) ? 1 : 2;
     static constexpr int STAGES = BN == 256 ? 3 : 4;  // measured at BN = 128: a fifth stage adds about 1 %
@@ -660,9 +664,9 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
             return __all_sync(0xffffffffu, mbar_wait(&ctrl->st_empty[handed % Cfg::SBUF], par ^ 1u, abort_flag,
                                                      p.status, kStatusTimeoutEpilogue));
         };
-        auto hand_over = [&](int tm, int tn, int kind) {
+        auto hand_over = [&](int tm, int tn, int kind, int half) {
             const int b = handed % Cfg::SBUF;
-            if (e == 0 && lane == 0) ctrl->st_meta[b] = make_int4(tm, tn, kind, 0);
+            if (e == 0 && lane == 0) ctrl->st_meta[b] = make_int4(tm, tn, kind, half);
             __syncwarp();
             if (lane == 0) mbar_arrive(&ctrl->st_full[b]);
             ++handed;
@@ -718,23 +722,35 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
                 }
                 ring.release(lane);
             }
-            // Stage the tile, rounded to the output type, for the store warps.
-            if (!take_staging()) break;
-            const int b = handed % Cfg::SBUF;
-            if (p.tma_store) {
-                // The bias (if any) goes on here, after the flag, to the product
-                // rounded to the output type.
-                const int col0 = tn * BN + colg * CW;
-                stage_row_swizzled<OUT, BM, CW>(staging + b * Cfg::STAGING_BYTES, q * 32 + lane, colg * CW, acc,
-                                                p.bias != nullptr ? p.bias + int64_t(col0) * p.sbias : nullptr,
-                                                p.sbias, p.N - col0);
-                fence_proxy_async_smem();  // the TMA store reads these bytes
-            } else {
-                stage_row<OUT, CW, Cfg::STAGE_PITCH>(staging + b * Cfg::STAGING_BYTES, q * 32 + lane, colg * CW, acc);
+            // Stage the tile, rounded to the output type, for the store warps (in
+            // HALVES column parts, one hand-over each; every epilogue warp takes
+            // part in each hand-over, staging only the part its columns are in).
+            bool staged = true;
+            for (int h = 0; h < Cfg::HALVES; ++h) {
+                if (!take_staging()) {
+                    staged = false;
+                    break;
+                }
+                const int b = handed % Cfg::SBUF;
+                if (Cfg::HALVES == 1 || colg * CW / Cfg::STAGE_COLS == h) {
+                    const int cin = colg * CW - h * Cfg::STAGE_COLS;  // column within the staged part
+                    if (p.tma_store) {
+                        // The bias (if any) goes on here, after the flag, to the product
+                        // rounded to the output type.
+                        const int col0 = tn * BN + colg * CW;
+                        stage_row_swizzled<OUT, BM, CW>(staging + b * Cfg::STAGING_BYTES, q * 32 + lane, cin, acc,
+                                                        p.bias != nullptr ? p.bias + int64_t(col0) * p.sbias : nullptr,
+                                                        p.sbias, p.N - col0);
+                        fence_proxy_async_smem();  // the TMA store reads these bytes
+                    } else {
+                        stage_row<OUT, CW, Cfg::STAGE_PITCH>(staging + b * Cfg::STAGING_BYTES, q * 32 + lane, cin, acc);
+                    }
+                }
+                const bool decide = inline_redo && main_item;
+                if (decide && bad && lane == 0) atomicOr(&ctrl->tile_bad[b], 1);
+                hand_over(tm, tn, decide ? kStoreDecide : kStoreTile, h);
             }
-            const bool decide = inline_redo && main_item;
-            if (decide && bad && lane == 0) atomicOr(&ctrl->tile_bad[b], 1);
-            hand_over(tm, tn, decide ? kStoreDecide : kStoreTile);
+            if (!staged) break;
         }
         if (CHUNKED && !finished) {
             // Leaving early (a wait gave up): raise the abort flag, then release the
@@ -745,7 +761,7 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
             __syncwarp();
             pairs.release_issued_on_exit(lane);
         }
-        if (finished && take_staging()) hand_over(0, 0, kStoreEnd);
+        if (finished && take_staging()) hand_over(0, 0, kStoreEnd, 0);
     } else {
         // ------------------------------------------------------------ store warps
         // Copy each staged tile out to C and to every peer's buffer (fused
@@ -769,6 +785,7 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
             const int4 m = ctrl->st_meta[b];
             if (m.z == kStoreEnd) break;
             const int tm = m.x, tn = m.y;
+            const int c0 = tn * BN + m.w * Cfg::STAGE_COLS;  // first column of the staged part
             bool redo_queued = false;  // this main tile is redone later in this CTA
             if (m.z == kStoreDecide && sw == 0 && lane == 0) {
                 if (atomicExch(&ctrl->tile_bad[b], 0) != 0) {
@@ -795,19 +812,19 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
                 if (sw == 0 && lane == 0) {
                     if (!redo_queued) {
 #pragma unroll
-                        for (int j = 0; j < BN / BOX_COLS; ++j)
-                            if (tn * BN + j * BOX_COLS < p.N)  // boxes wholly past the last column hold nothing
-                                tma_store_2d(&p.tmC, stg + j * (BM * 128), tn * BN + j * BOX_COLS, tm * BM);
+                        for (int j = 0; j < Cfg::STAGE_COLS / BOX_COLS; ++j)
+                            if (c0 + j * BOX_COLS < p.N)  // boxes wholly past the last column hold nothing
+                                tma_store_2d(&p.tmC, stg + j * (BM * 128), c0 + j * BOX_COLS, tm * BM);
                         bulk_commit_group();
                         bulk_wait_group_read0();  // the staging tile may be reused once read
                     }
                 }
             } else if (p.c_vec)
-                store_staged<OUT, BM, BN, Cfg::STAGE_PITCH, Cfg::STORE_WARPS>(
-                    stg, dsts, 1 + p.n_peers, p.sCm, tm * BM, tn * BN, p.M, p.N, sw, lane, p.bias, p.sbias);
+                store_staged<OUT, BM, Cfg::STAGE_COLS, Cfg::STAGE_PITCH, Cfg::STORE_WARPS>(
+                    stg, dsts, 1 + p.n_peers, p.sCm, tm * BM, c0, p.M, p.N, sw, lane, p.bias, p.sbias);
             else
-                store_staged_strided<OUT, BM, BN, Cfg::STAGE_PITCH, Cfg::STORE_WARPS>(
-                    stg, dsts, 1 + p.n_peers, p.sCm, p.sCn, tm * BM, tn * BN, p.M, p.N, sw, lane, p.bias, p.sbias);
+                store_staged_strided<OUT, BM, Cfg::STAGE_COLS, Cfg::STAGE_PITCH, Cfg::STORE_WARPS>(
+                    stg, dsts, 1 + p.n_peers, p.sCm, p.sCn, tm * BM, c0, p.M, p.N, sw, lane, p.bias, p.sbias);
             __syncwarp();
             if (lane == 0) mbar_arrive(&ctrl->st_empty[b]);  // the staging tile is free again
         }

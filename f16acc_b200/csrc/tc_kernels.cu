@@ -60,14 +60,16 @@ cudaError_t launch_shape(const TcParams& p, bool chunked, bool b_mn, int out, bo
     return cudaErrorInvalidValue;
 }
 
-// 128x256 tiles: FP32 mode (no flags, no redo) with a 2-byte C only.
+// 128x256 tiles: FP32 mode (no flags, no redo).
 cudaError_t launch_wide_fp32(const TcParams& p, bool b_mn, int out, int grid, cudaStream_t stream) {
     if (b_mn) {
         if (out == kOutF16) return launch_one<256, 4, false, true, kOutF16, false>(p, grid, stream);
         if (out == kOutBF16) return launch_one<256, 4, false, true, kOutBF16, false>(p, grid, stream);
+        if (out == kOutF32) return launch_one<256, 4, false, true, kOutF32, false>(p, grid, stream);
     } else {
         if (out == kOutF16) return launch_one<256, 4, false, false, kOutF16, false>(p, grid, stream);
         if (out == kOutBF16) return launch_one<256, 4, false, false, kOutBF16, false>(p, grid, stream);
+        if (out == kOutF32) return launch_one<256, 4, false, false, kOutF32, false>(p, grid, stream);
     }
     return cudaErrorInvalidValue;
 }

@@ -154,8 +154,8 @@ int f16acc_gemm_allgather(const void *A, int64_t sAm, int64_t sAk,
  * launching: variant (F16ACC_VARIANT_TCGEN05 or _MMA_SYNC), output tile shape,
  * and the tile grid of the flags (flag slot of tile (tm, tn) = tm * tiles_n +
  * tn, each slot f16acc_flag_bytes_per_tile() bytes, non-zero bytes =
- * flagged).  A chunked == 0 call on the tcgen05 variant into a 2-byte C with
- * N >= 256 runs on 128x256 tiles; it writes no flags. */
+ * flagged).  A chunked == 0 call on the tcgen05 variant with N >= 256 may run
+ * on 128x256 tiles (f16acc_set_fp32_tiles); it writes no flags. */
 typedef struct f16acc_plan {
     int variant;
     int tile_m, tile_n;
@@ -170,8 +170,7 @@ int f16acc_flag_bytes_per_tile(void);
  * per tile (128) and epilogue column slices per TMEM lane quarter (2 or 4,
  * i.e. 8 or 16 epilogue warps; 0 = the default, 2 for chunked accumulation
  * and 4 for FP32 accumulation).  It does not apply to the 128x256 tiles of
- * chunked == 0 calls into a 2-byte C.  A tuning knob; results do not depend
- * on it. */
+ * chunked == 0 calls.  A tuning knob; results do not depend on it. */
 int f16acc_set_tc_config(int tile_n, int epi_split);
 
 /* Cap the SMs a GEMM launch occupies, process-wide, for later calls (0 = all
@@ -204,8 +203,8 @@ int f16acc_set_redo_mode(int mode);
 #define F16ACC_SCHEDULE_DYNAMIC 1
 int f16acc_set_schedule(int mode);
 
-/* Tile width of FP32-mode calls (chunked == 0) into a 2-byte C, process-wide,
- * for later calls: F16ACC_FP32_TILES_AUTO (the default) takes 128x256 tiles
+/* Tile width of FP32-mode calls (chunked == 0), process-wide, for later
+ * calls: F16ACC_FP32_TILES_AUTO (the default) takes 128x256 tiles
  * when N >= 256 and they finish in fewer modelled tile-times than 128x128
  * ones (a wide tile costs about 1.5 narrow ones), F16ACC_FP32_TILES_WIDE takes
  * them whenever N >= 256, F16ACC_FP32_TILES_NARROW never.  Every output

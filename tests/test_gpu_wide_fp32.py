@@ -1,7 +1,7 @@
-"""FP32 mode (`chunked=False`) into a 2-byte C with N >= 256 may run on
-128x256 tiles (f16acc_set_fp32_tiles: by a wave model, always, or never);
-every other FP32-mode call (fp32 C, N < 256, the redo of flagged tiles) runs on
-128x128 tiles.  Both issue the same K16 MMA sequence per output element, so
+"""FP32 mode (`chunked=False`) with N >= 256 may run on 128x256 tiles
+(f16acc_set_fp32_tiles: by a wave model, always, or never; an fp32 C is
+staged in two column halves); every other FP32-mode call (N < 256, the redo
+of flagged tiles) runs on 128x128 tiles.  Both issue the same K16 MMA sequence per output element, so
 the results must be identical bit for bit (f16acc/kernel.py:50-51: one FP32
 accumulator over all of K, then the cast), and within FP32 accumulation error
 of an FP64 product."""
@@ -49,7 +49,7 @@ def operands(M, N, K, layout, cuda, seed):
     return a, b
 
 
-@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16], ids=str)
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16, torch.float32], ids=str)
 @pytest.mark.parametrize("layout", ["row_major", "w_t"])
 @pytest.mark.parametrize("M,N,K", SHAPES, ids=[f"{m}x{n}x{k}" for m, n, k in SHAPES])
 def test_wide_tiles_equal_the_128_wide_fp32_path(cuda, M, N, K, layout, out_dtype):
@@ -68,17 +68,35 @@ def test_wide_tiles_equal_the_128_wide_fp32_path(cuda, M, N, K, layout, out_dtyp
     assert err <= ref.abs().max().item() * F32_TOL
 
 
-def test_wide_tiles_strided_output(cuda):
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32], ids=str)
+def test_wide_tiles_strided_output(cuda, out_dtype):
     """A column-major C leaves through the store warps' element-wise copy-out
     instead of TMA stores."""
-    M, N, K = 384, 768, 320
+    M, N, K = 384, 776, 320
     a, b = operands(M, N, K, "w_t", cuda, seed=9)
-    out = torch.empty(N, M, device=cuda, dtype=torch.float16).t()
+    out = torch.empty(N, M, device=cuda, dtype=out_dtype).t()
     with fp32_tiles(_lib.FP32_TILES_WIDE):
-        c, _ = mm_ex(a, b, torch.float16, chunked=False, out=out)
+        c, _ = mm_ex(a, b, out_dtype, chunked=False, out=out)
     assert c.data_ptr() == out.data_ptr()
-    narrow = mm(a, b, torch.float32, chunked=False)
-    assert torch.equal(c, narrow.half())
+    with fp32_tiles(_lib.FP32_TILES_NARROW):
+        narrow = mm(a, b, torch.float32, chunked=False)
+    assert torch.equal(c, narrow.to(out_dtype))
+
+
+def test_wide_tiles_bias(cuda):
+    """The bias goes on in the epilogue of the wide tiles too, bit-equal to
+    the product rounded to C's type and then y += b."""
+    from f16acc_b200.kernel import mm_bias
+
+    M, N, K = 256, 1032, 256
+    a, b = operands(M, N, K, "w_t", cuda, seed=11)
+    bias = torch.randn(N, device=cuda).half()
+    for dt in (torch.float16, torch.float32):
+        with fp32_tiles(_lib.FP32_TILES_WIDE):
+            fused = mm_bias(a, b, bias, dt, chunked=False)
+            ref = mm(a, b, dt, chunked=False)
+        ref = (ref.float() + bias.float()).to(dt)
+        assert torch.equal(fused, ref)
 
 
 def test_wide_tiles_match_redone_tiles(cuda):
