@@ -56,24 +56,25 @@ cudaError_t ensure_smem_attr(Kernel kernel, int smem) {
     return ensure_smem_attr_raw(reinterpret_cast<const void*>(kernel), smem);
 }
 
-// Launch helper: cudaLaunchKernelEx with optional programmatic stream
-// serialisation (the dependent kernel may start its prologue while the
-// previous kernel on the stream drains; it calls griddepcontrol.wait before
-// touching that kernel's results).
+// Launch helper: cudaLaunchKernelEx with programmatic stream serialisation.
+// Every GEMM kernel is launched this way: its CTAs may start their prologue
+// while the previous kernel on the stream drains (once that kernel's CTAs have
+// all run griddepcontrol.launch_dependents, or exited), and each calls
+// griddepcontrol.wait before its first global-memory access, which returns
+// when the previous kernel has completed and its writes are visible.  Behind
+// a kernel that never triggers, the launch waits for its completion as usual.
 template <typename Kernel, typename Params>
-cudaError_t launch_ex(Kernel kernel, const Params& p, int grid, int threads, int smem, cudaStream_t stream, bool pdl) {
+cudaError_t launch_ex(Kernel kernel, const Params& p, int grid, int threads, int smem, cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
     cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
     cfg.dynamicSmemBytes = static_cast<size_t>(smem);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
-    if (pdl) {
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-    }
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 

@@ -100,8 +100,9 @@ __global__ void __launch_bounds__(MmaCfg::THREADS) mma_gemm_kernel(const __grid_
     const int wm = warp >> 2, wn = warp & 3;  // warp tile origin: rows wm*64, cols wn*32
     const int g = lane >> 2, tq = lane & 3;   // mma fragment coordinates
 
-    if constexpr (REDO) grid_dep_wait();
-    else grid_dep_launch();
+    // programmatic dependent launch: nothing above touches global memory
+    grid_dep_wait();
+    if constexpr (!REDO) grid_dep_launch();
 
     const int tiles = p.tiles_m * p.tiles_n;
     const int nkt = (p.K + BK - 1) / BK;  // one chunk per K step

@@ -9,8 +9,7 @@ namespace {
 
 template <bool CHUNKED, int A_MODE, int B_MODE, int OUT, bool REDO>
 cudaError_t launch_one(const MmaParams& p, int grid, cudaStream_t stream) {
-    return launch_ex(mma_gemm_kernel<CHUNKED, A_MODE, B_MODE, OUT, REDO>, p, grid, MmaCfg::THREADS, 0, stream,
-                     /*pdl=*/REDO);
+    return launch_ex(mma_gemm_kernel<CHUNKED, A_MODE, B_MODE, OUT, REDO>, p, grid, MmaCfg::THREADS, 0, stream);
 }
 
 template <int A_MODE, int B_MODE, int OUT>

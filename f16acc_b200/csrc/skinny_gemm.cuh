@@ -307,8 +307,11 @@ __global__ void __launch_bounds__(SkinnyCfg::THREADS) skinny_gemm_kernel(const _
     const int k_begin = rank * p.kper;
     const int k_end = min(p.K, k_begin + p.kper);
 
+    // Programmatic dependent launch (as every GEMM kernel here): nothing above
+    // touches global memory; the wait returns once the previous kernel on the
+    // stream (for the redo pass: the chunked pass, its flags and C) is complete.
+    grid_dep_wait();
     if constexpr (REDO) {
-        grid_dep_wait();  // the chunked pass's flags and C
         if (!tile_flagged(p.flags, tile)) return;  // every CTA of the cluster reads the same flag
     } else {
         grid_dep_launch();

@@ -24,14 +24,10 @@ cudaError_t launch_one(const SkinnyParams& p, int tiles_n, int splits, cudaStrea
     attr[0].val.clusterDim.x = 1;
     attr[0].val.clusterDim.y = static_cast<unsigned>(splits);
     attr[0].val.clusterDim.z = 1;
-    int n = 1;
-    if (REDO) {
-        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[1].val.programmaticStreamSerializationAllowed = 1;
-        n = 2;
-    }
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // the kernel waits before global access
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = n;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 

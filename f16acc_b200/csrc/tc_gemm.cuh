@@ -332,11 +332,14 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
     tc_fence_after();
     const uint32_t tmem = ctrl->tmem_slot;
 
-    if constexpr (REDO) {
-        grid_dep_wait();  // flags and C come from the main pass
-    } else {
-        grid_dep_launch();  // let the redo pass get scheduled as early as possible
-    }
+    // Every launch is a programmatic dependent launch: the CTAs may start while
+    // the previous kernel on the stream drains, and everything above (barriers,
+    // TMEM, descriptor prefetch) touches no global memory.  griddepcontrol.wait
+    // returns once that kernel has completed and its writes are visible (the
+    // redo pass: the main pass's flags and C).  The main pass then lets the
+    // next launch on the stream get scheduled.
+    grid_dep_wait();
+    if constexpr (!REDO) grid_dep_launch();
 
     const int tiles = p.tiles_m * p.tiles_n;
     const int nkb = (p.K + BK - 1) / BK;

@@ -32,7 +32,7 @@ cudaError_t launch_one(const TcParams& p, int grid, cudaStream_t stream) {
     auto kernel = tc_gemm_kernel<BN, EPI, CHUNKED, B_MN, OUT, REDO>;
     cudaError_t e = ensure_smem_attr(kernel, Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    return launch_ex(kernel, p, grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream, /*pdl=*/REDO);
+    return launch_ex(kernel, p, grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream);
 }
 
 template <int BN, int EPI, bool B_MN, int OUT>
