@@ -44,6 +44,7 @@ SIGNATURES = {
     "f16acc_set_redo_mode": (_int, [_int]),
     "f16acc_set_schedule": (_int, [_int]),
     "f16acc_set_fp32_tiles": (_int, [_int]),
+    "f16acc_set_tail_split": (_int, [_int]),
     "f16acc_probe_chunk_rate": (_int, [_int, _int, _int, _int, _p, _int, _p]),
     "f16acc_selftest_wait_timeout": (_int, [ctypes.c_uint64, _p, _int, _p]),
     "f16acc_device_status": (_int, [_int, _int]),
@@ -68,6 +69,7 @@ VARIANT_NAMES = {VARIANT_AUTO: "auto", VARIANT_TCGEN05: "tcgen05", VARIANT_MMA_S
 REDO_SEPARATE, REDO_INLINE = 0, 1
 SCHEDULE_STATIC, SCHEDULE_DYNAMIC = 0, 1
 FP32_TILES_AUTO, FP32_TILES_WIDE, FP32_TILES_NARROW = 0, 1, 2
+TAIL_SPLIT_OFF, TAIL_SPLIT_ON = 0, 1
 
 _lib = None
 _lock = threading.Lock()

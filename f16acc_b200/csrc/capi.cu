@@ -161,6 +161,49 @@ std::atomic<int> g_schedule{F16ACC_SCHEDULE_DYNAMIC};
 std::atomic<int> g_fp32_tiles{F16ACC_FP32_TILES_AUTO};
 constexpr int kGroupM = 8;
 
+// Tail split of the chunked tcgen05 main pass (F16ACC_TAIL_SPLIT_*).  The
+// tiles past the last full wave of the SMs (all of them when there are fewer
+// tiles than SMs) run as S units over contiguous shares of K: S = the units
+// that still fit beside each other on the SMs, at most kSplitMax, each unit at
+// least kSplitMinStages 64-wide stages.  A split costs about 8-11 us on the
+// critical path (the counter reset, each unit's pipeline fill and partial
+// write, the last unit's read-back), measured on shapes from 1024^3 to the
+// Qwen projections, against about 0.39 us per 64-wide stage it takes off a
+// tile; so it is used only when it takes at least kSplitMinSaved stages off.
+std::atomic<int> g_tail_split{F16ACC_TAIL_SPLIT_ON};
+constexpr int64_t kSplitMax = 4;
+constexpr int64_t kSplitMinStages = 6;
+constexpr int64_t kSplitMinSaved = 32;
+constexpr int64_t kSplitSlots = 148;  // partial tiles at most: S x split tiles <= SMs
+constexpr int64_t kSplitPartialBytes = 128 * 128 * 4;
+
+struct TailSplit {
+    int64_t s = 0, first = 0, tiles = 0;  // parts, first split tile, split tiles
+};
+TailSplit plan_split(int64_t tiles, int64_t K, int64_t sms) {
+    TailSplit t;
+    const int64_t nkb = cdiv(K, 64);
+    const int64_t r = tiles < sms ? tiles : tiles % sms;
+    if (r <= 0) return t;
+    int64_t S = sms / r;
+    if (S > kSplitMax) S = kSplitMax;
+    if (S > nkb / kSplitMinStages) S = nkb / kSplitMinStages;
+    if (S < 2 || S * r > kSplitSlots || nkb - nkb / S < kSplitMinSaved) return t;
+    t.s = S;
+    t.first = tiles - r;
+    t.tiles = r;
+    return t;
+}
+// Workspace layout: the flags (kFlagBytesPerTile a tile), then, when a tail
+// split can happen, one counter per split tile and the partial tiles.
+int64_t flag_area(int64_t M, int64_t N) { return cdiv(M, 128) * cdiv(N, 128) * kFlagBytesPerTile; }
+int64_t split_counters_at(int64_t M, int64_t N) { return cdiv(flag_area(M, N), 256) * 256; }
+int64_t split_partials_at(int64_t M, int64_t N) { return split_counters_at(M, N) + kSplitSlots * 4 + 512; }
+bool split_possible(int64_t M, int64_t N, int64_t K) {
+    const int64_t nkb = cdiv(K, 64);
+    return M > 0 && N > 0 && nkb / kSplitMax >= kSplitMinStages && nkb - nkb / kSplitMax >= kSplitMinSaved;
+}
+
 // Rows up to which the few-row kernel is the automatic choice: 64, except
 // for very wide products (lm_head-sized N), where at 64 rows the tcgen05
 // kernel is faster (measured on the 1536 x 151936 weight: 110 against 148 us);
@@ -237,7 +280,8 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
     int v = choose_variant(L, M, N, K, variant, n_peers > 0);
     if (v < 0) return variant == F16ACC_VARIANT_AUTO ? F16ACC_ERR_INVALID_ARGUMENT : F16ACC_ERR_UNSUPPORTED;
     if (chunked) {
-        if (workspace == nullptr || ws_bytes < f16acc_workspace_bytes(M, N, K) ||
+        // The flags must fit; the tail split's area is used only when it fits too.
+        if (workspace == nullptr || ws_bytes < size_t(flag_area(M, N)) ||
             reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
             return F16ACC_ERR_WORKSPACE;
     }
@@ -338,20 +382,40 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
         const int64_t tiles = int64_t(p.tiles_m) * p.tiles_n;
         if (tiles >= (int64_t(1) << 31)) return F16ACC_ERR_INVALID_ARGUMENT;
         const int sms = usable_sms(info->sms);
-        const int grid = int(tiles < sms ? tiles : sms);
+        // Tail split of the chunked main pass, when the caller's workspace holds
+        // its counters and partials; the counters start at zero.
+        int64_t units = tiles;
+        if (chunked && (phases & kPhaseMain) && bn == 128 &&
+            g_tail_split.load(std::memory_order_relaxed) == F16ACC_TAIL_SPLIT_ON && split_possible(M, N, K)) {
+            const TailSplit t = plan_split(tiles, K, sms);
+            const int64_t need = split_partials_at(M, N) + t.s * t.tiles * kSplitPartialBytes;
+            if (t.s >= 2 && int64_t(ws_bytes) >= need) {
+                uint8_t* ws = static_cast<uint8_t*>(workspace);
+                p.split_s = int(t.s);
+                p.split_first = int(t.first);
+                units = t.first + t.tiles * t.s;
+                p.units = int(units);
+                p.split_cnt = reinterpret_cast<int*>(ws + split_counters_at(M, N));
+                p.split_part = reinterpret_cast<float*>(ws + split_partials_at(M, N));
+                if (cudaMemsetAsync(p.split_cnt, 0, size_t(t.tiles) * sizeof(int), stream) != cudaSuccess)
+                    return F16ACC_ERR_CUDA;
+            }
+        }
+        const int grid = int(units < sms ? units : sms);
         // Both passes in one launch when the caller wants both.
         p.inline_redo = chunked && phases == kPhaseBoth &&
                         g_redo_mode.load(std::memory_order_relaxed) == F16ACC_REDO_INLINE;
         // The chunked main pass takes its tiles dynamically (one CTA launched per
         // tile, running CTAs take over the tiles of CTAs not started yet) unless
         // an SM cap asks for a bounded persistent grid.
-        p.dyn_sched = chunked && tiles > grid && g_sm_limit.load(std::memory_order_relaxed) == 0 &&
+        p.dyn_sched = chunked && units > grid && g_sm_limit.load(std::memory_order_relaxed) == 0 &&
                       g_schedule.load(std::memory_order_relaxed) == F16ACC_SCHEDULE_DYNAMIC;
         if ((phases & kPhaseMain) &&
-            launch_tc(p, shape, chunked != 0, b_mn, c_dtype, false, p.dyn_sched ? int(tiles) : grid, stream) !=
+            launch_tc(p, shape, chunked != 0, b_mn, c_dtype, false, p.dyn_sched ? int(units) : grid, stream) !=
                 cudaSuccess)
             return F16ACC_ERR_CUDA;
-        p.dyn_sched = 0;  // the separate redo pass walks the flags in static order
+        p.dyn_sched = 0;  // the separate redo pass walks the flags in static order, whole tiles
+        p.split_s = 0;
         if (chunked && (phases & kPhaseRedo) && !p.inline_redo &&
             launch_tc(p, tc_shape(false), false, b_mn, c_dtype, true, grid, stream) != cudaSuccess)
             return F16ACC_ERR_CUDA;
@@ -449,11 +513,13 @@ int f16acc_gemm_bias(const void* A, int64_t sAm, int64_t sAk, const void* B, int
 }
 
 size_t f16acc_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-    (void)K;
     if (M <= 0 || N <= 0) return 16;
-    // Smallest tile any variant uses is 128 x 128.
+    // Smallest tile any variant uses is 128 x 128: its flags, then room for the
+    // tail split (at most kSplitSlots partial tiles, and 4 a tile).
+    if (!split_possible(M, N, K)) return size_t(flag_area(M, N));
     const int64_t tiles = cdiv(M, 128) * cdiv(N, 128);
-    return size_t(tiles) * kFlagBytesPerTile;
+    const int64_t slots = tiles * kSplitMax < kSplitSlots ? tiles * kSplitMax : kSplitSlots;
+    return size_t(split_partials_at(M, N) + slots * kSplitPartialBytes);
 }
 
 const char* f16acc_strerror(int code) {
@@ -528,6 +594,11 @@ int f16acc_set_redo_mode(int mode) {
 int f16acc_set_schedule(int mode) {
     if (mode != F16ACC_SCHEDULE_STATIC && mode != F16ACC_SCHEDULE_DYNAMIC) return F16ACC_ERR_INVALID_ARGUMENT;
     return g_schedule.exchange(mode);
+}
+
+int f16acc_set_tail_split(int mode) {
+    if (mode != F16ACC_TAIL_SPLIT_ON && mode != F16ACC_TAIL_SPLIT_OFF) return F16ACC_ERR_INVALID_ARGUMENT;
+    return g_tail_split.exchange(mode);
 }
 
 int f16acc_set_fp32_tiles(int mode) {

@@ -77,10 +77,12 @@ extern "C" int f16acc_gemm_noalloc(const void* A, int64_t sAm, int64_t sAk, cons
     if (!chunked || M == 0 || N == 0 || K == 0)
         return f16acc_gemm(A, sAm, sAk, B, sBk, sBn, C, sCm, sCn, c_dtype, M, N, K, chunked, nullptr, 0, device,
                            stream);
-    const size_t need = f16acc_workspace_bytes(M, N, K);
+    // The flags of every 128 x 128 output tile, and no more: handed a workspace
+    // that holds only the flags, f16acc_gemm runs without the tail split.
+    const size_t need = size_t((M + 127) / 128) * size_t((N + 127) / 128) * 16;
     if (need > f16acc::kNoAllocFlagBytes) return F16ACC_ERR_TOO_LARGE;
     void* flags = f16acc::scratch_for(device);
     if (flags == nullptr) return F16ACC_ERR_CUDA;
-    return f16acc_gemm(A, sAm, sAk, B, sBk, sBn, C, sCm, sCn, c_dtype, M, N, K, chunked, flags,
-                       f16acc::kNoAllocFlagBytes, device, stream);
+    return f16acc_gemm(A, sAm, sAk, B, sBk, sBn, C, sCm, sCn, c_dtype, M, N, K, chunked, flags, need, device,
+                       stream);
 }

@@ -78,7 +78,43 @@ struct TcParams {
     // CTA takes over the tile of a CTA not yet started (cluster launch
     // control), so a CTA slowed by redo work takes fewer main tiles.
     int dyn_sched;
+    // Tail split (chunked main pass): the tiles from split_first on (those past
+    // the last full wave of the SMs) run as split_s work units each, unit s
+    // over the s-th contiguous share of the 64-wide K stages.  Each unit leaves
+    // its FP32 partial tile in split_part; the unit that finishes last (counted
+    // in split_cnt, zeroed before the launch) adds the tile's partials in part
+    // order, then flags and stores the tile like a whole one.  split_s < 2: no
+    // split, units = tiles.
+    int split_s;
+    int split_first;
+    int units;
+    int* split_cnt;      // one counter per split tile
+    float* split_part;   // [split tile][part][epilogue warp][CW / 4][32 lanes] float4
 };
+
+// Work unit u: its tile and its part code, -1 for the whole K range, else
+// (split tile index << 3) | part.
+__device__ __forceinline__ void unit_tile(const TcParams& p, int u, int& tm, int& tn, int& part) {
+    int t = u;
+    part = -1;
+    if (p.split_s > 1 && u >= p.split_first) {
+        const int j = u - p.split_first;
+        t = p.split_first + j / p.split_s;
+        part = ((j / p.split_s) << 3) | (j % p.split_s);
+    }
+    raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+}
+// The 64-wide K stages [kb0, kb1) of a work unit.
+__device__ __forceinline__ void unit_stages(const TcParams& p, int part, int nkb, int& kb0, int& kb1) {
+    if (part < 0) {
+        kb0 = 0;
+        kb1 = nkb;
+    } else {
+        const int s = part & 7;
+        kb0 = s * nkb / p.split_s;
+        kb1 = (s + 1) * nkb / p.split_s;
+    }
+}
 
 // Work items the producer warp hands to the MMA warp and the epilogue.
 enum TcWork : int { kWorkMain = 0, kWorkRedo = 1, kWorkEnd = 2 };
@@ -89,7 +125,7 @@ constexpr int kRedoQueue = 32;   // flagged tiles waiting for their FP32 redo (b
 template <int STAGES, int NBUF>
 struct alignas(16) TcCtrl {
     uint4 clc_resp;                    // cluster launch control response
-    int4 sched[kSchedDepth];           // {tm, tn, kind, 0}
+    int4 sched[kSchedDepth];           // {tm, tn, kind, part code}
     int2 redo_q[kRedoQueue];           // {tm, tn} of flagged tiles
     uint64_t full[STAGES], empty[STAGES];
     uint64_t tfull[NBUF], tempty[NBUF];
@@ -103,6 +139,11 @@ struct alignas(16) TcCtrl {
     int rq_head;                       // redo items taken (producer)
     int main_done;                     // main tiles whose flag is decided (store warps)
     int tile_bad[2];                   // OR of the epilogue warps' flags for the tile in staging b
+    // Tail split: every epilogue warp has written its slice of the unit's
+    // partial (split_written), and epilogue warp 0 has counted the unit in
+    // (split_decided; split_last: it was the tile's last unit).
+    uint64_t split_written, split_decided;
+    int split_last;
 };
 
 // What a staged tile asks of the store warps.
@@ -110,6 +151,7 @@ enum TcStore : int {
     kStoreTile = 0,     // copy it out
     kStoreDecide = 1,   // copy it out, and decide whether it needs the in-kernel FP32 redo
     kStoreEnd = 2,      // no tile: the epilogue is done
+    kStoreNone = 3,     // no tile: a split unit that was not its tile's last (its main item is done)
 };
 
 template <int BN_, int EPI_SPLIT_, int OUT_, bool CHUNKED_>
@@ -310,6 +352,8 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
         }
         mbar_init(&ctrl->clc_bar, 1);
         mbar_init(drain, ISSUERS);
+        mbar_init(&ctrl->split_written, Cfg::EPI_WARPS);
+        mbar_init(&ctrl->split_decided, 1);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&ctrl->st_full[b], Cfg::EPI_WARPS);
             mbar_init(&ctrl->st_empty[b], Cfg::STORE_WARPS);
@@ -342,6 +386,7 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
     if constexpr (!REDO) grid_dep_launch();
 
     const int tiles = p.tiles_m * p.tiles_n;
+    const int units = p.split_s > 1 ? p.units : tiles;  // work units of the main pass
     const int nkb = (p.K + BK - 1) / BK;
     const int nchunks = (p.K + 31) / 32;
     const int nk16 = (p.K + 15) / 16;
@@ -351,8 +396,10 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
         if (lane == 0) {
             uint32_t s = 0, ph = 0;
             uint32_t pending = 0, pend_parity = 0;  // stages with a load issued, and that load's phase parity
-            auto load_tile = [&](int tm, int tn) -> bool {
-                for (int kb = 0; kb < nkb; ++kb) {
+            auto load_tile = [&](int tm, int tn, int part) -> bool {
+                int kb0, kb1;
+                unit_stages(p, part, nkb, kb0, kb1);
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.status, kStatusTimeoutProducer)) return false;
                     mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
                     pending |= 1u << s;
@@ -373,7 +420,7 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
             // ---- tile scheduler: this thread decides the CTA's work items, in order,
             // and publishes each to the MMA warp and the epilogue through ctrl->sched.
             const bool inline_redo = CHUNKED && p.inline_redo != 0;
-            int next_static = blockIdx.x;  // static order: this CTA's next main tile
+            int next_static = blockIdx.x;  // static order: this CTA's next main work unit
             bool clc_inflight = false;     // a cancel request not yet answered
             uint32_t clc_phase = 0;
             int issued_main = 0, taken = 0;
@@ -408,8 +455,9 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
             // The next work item: a finished flagged tile's redo first, then a new
             // main tile, then (main tiles exhausted) the redo items still to come,
             // then the end.  False when a wait gave up.
-            auto next_work = [&](int& kind, int& tm, int& tn) -> bool {
+            auto next_work = [&](int& kind, int& tm, int& tn, int& part) -> bool {
                 kind = kWorkRedo;
+                part = -1;
                 if (inline_redo && pop_redo(tm, tn)) return true;
                 kind = kWorkMain;
                 if (p.dyn_sched) {
@@ -419,22 +467,23 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
                         clc_phase ^= 1u;
                         clc_inflight = false;
                         uint32_t cta;
-                        if (clc_query(&ctrl->clc_resp, cta)) {  // that CTA's tile is ours now
+                        if (clc_query(&ctrl->clc_resp, cta)) {  // that CTA's work unit is ours now
                             clc_ask();
-                            raster(static_cast<int>(cta), p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+                            unit_tile(p, static_cast<int>(cta), tm, tn, part);
                             return true;
                         }
                     }
                 } else {
-                    while (next_static < tiles) {
+                    while (next_static < units) {
                         const int t = next_static;
                         next_static += gridDim.x;
-                        raster(t, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+                        unit_tile(p, t, tm, tn, part);
                         if (REDO && !tile_flagged(p.flags, static_cast<int64_t>(tm) * p.tiles_n + tn)) continue;
                         return true;
                     }
                 }
                 kind = kWorkRedo;
+                part = -1;
                 if (inline_redo) {
                     if (!wait_flags_decided()) return false;
                     if (pop_redo(tm, tn)) return true;
@@ -442,24 +491,24 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
                 kind = kWorkEnd;
                 return true;
             };
-            int kind, tm, tn;
-            if (p.dyn_sched) {  // this CTA's own tile first, the next one asked for meanwhile
+            int kind, tm, tn, part;
+            if (p.dyn_sched) {  // this CTA's own work unit first, the next one asked for meanwhile
                 kind = kWorkMain;
-                raster(blockIdx.x, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
+                unit_tile(p, static_cast<int>(blockIdx.x), tm, tn, part);
                 clc_ask();
-            } else if (!next_work(kind, tm, tn)) {
+            } else if (!next_work(kind, tm, tn, part)) {
                 goto producer_done;
             }
             for (uint32_t qi = 0, qph = 0;;) {
                 if (!mbar_wait(&ctrl->sched_empty[qi], qph ^ 1u, abort_flag, p.status, kStatusTimeoutProducer))
                     goto producer_done;
-                ctrl->sched[qi] = make_int4(tm, tn, kind, 0);
+                ctrl->sched[qi] = make_int4(tm, tn, kind, part);
                 mbar_arrive(&ctrl->sched_full[qi]);
                 if (++qi == kSchedDepth) { qi = 0; qph ^= 1u; }
                 if (kind == kWorkEnd) break;
                 if (kind == kWorkMain) ++issued_main;
-                if (!load_tile(tm, tn)) goto producer_done;
-                if (!next_work(kind, tm, tn)) goto producer_done;
+                if (!load_tile(tm, tn, part)) goto producer_done;
+                if (!next_work(kind, tm, tn, part)) goto producer_done;
             }
         producer_done:
             // Let every copy this CTA issued land before the CTA can exit
@@ -560,6 +609,7 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
             for (uint32_t qi = 0, qph = 0;;) {
                 if (!wait(&ctrl->sched_full[qi], qph)) goto mma_done;
                 const int kind = ctrl->sched[qi].z;
+                const int part = ctrl->sched[qi].w;
                 if constexpr (CHUNKED) __syncwarp();
                 if (issue) mbar_arrive(&ctrl->sched_empty[qi]);
                 if (++qi == kSchedDepth) { qi = 0; qph ^= 1u; }
@@ -584,9 +634,12 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
                     }
                     b ^= 1u;
                 } else if constexpr (CHUNKED) {
-                    // One hand-off per 64-wide stage: its two 32-long chunks go to the
-                    // chunk buffers 2b and 2b+1 of pair b, issued by warp 1 + b.
-                    for (int kb = 0; kb < nkb; ++kb) {
+                    // One hand-off per 64-wide stage of the work unit: its two 32-long
+                    // chunks go to the chunk buffers 2b and 2b+1 of pair b, issued by
+                    // warp 1 + b.
+                    int kb0, kb1;
+                    unit_stages(p, part, nkb, kb0, kb1);
+                    for (int kb = kb0; kb < kb1; ++kb) {
                         if (b == mine) {
                             if (!wait(&full[s], ph)) goto mma_done;
                             // operands and accumulators of this hand-off, worked out before
@@ -675,6 +728,63 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
             ++handed;
         };
         const bool inline_redo = CHUNKED && p.inline_redo != 0;
+        // Tail split: leave this warp's slice of the unit's FP32 partial in
+        // split_part, count the unit in once every epilogue warp has written,
+        // and, in the tile's last unit, replace acc with the tile's total
+        // ((p0 + p1) + p2) + ... in part order, so the sum does not depend on
+        // which unit finishes last.  1: last (acc holds the total), 0: not the
+        // last, -1: a wait gave up.
+        uint32_t split_phase = 0;
+        auto split_combine = [&](int code, float (&a)[CW]) -> int {
+            const int ts = code >> 3, S = p.split_s;
+            auto slot = [&](int part) {
+                return reinterpret_cast<float4*>(p.split_part) +
+                       ((int64_t(ts) * S + part) * Cfg::EPI_WARPS + e) * (CW / 4) * 32 + lane;
+            };
+            float4* mine = slot(code & 7);
+#pragma unroll
+            for (int j = 0; j < CW / 4; ++j)
+                __stcg(mine + j * 32, make_float4(a[4 * j], a[4 * j + 1], a[4 * j + 2], a[4 * j + 3]));
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctrl->split_written);
+            const uint32_t par = split_phase & 1u;
+            ++split_phase;
+            if (!__all_sync(0xffffffffu, mbar_wait(&ctrl->split_written, par, abort_flag, p.status,
+                                                   kStatusTimeoutEpilogue)))
+                return -1;
+            if (e == 0 && lane == 0) {
+                __threadfence();  // every epilogue warp's partial is visible before the count
+                ctrl->split_last = atomicAdd(p.split_cnt + ts, 1) == S - 1 ? 1 : 0;
+                mbar_arrive(&ctrl->split_decided);
+            }
+            if (!__all_sync(0xffffffffu, mbar_wait(&ctrl->split_decided, par, abort_flag, p.status,
+                                                   kStatusTimeoutEpilogue)))
+                return -1;
+            if (*reinterpret_cast<volatile int*>(&ctrl->split_last) == 0) return 0;
+            __threadfence();  // the other units' partials, counted in before this one
+#pragma unroll
+            for (int j = 0; j < CW / 4; ++j) {
+                const float4 v = __ldcg(slot(0) + j * 32);
+                a[4 * j] = v.x;
+                a[4 * j + 1] = v.y;
+                a[4 * j + 2] = v.z;
+                a[4 * j + 3] = v.w;
+            }
+            for (int part = 1; part < S; ++part) {
+                float4 v[CW / 4];
+#pragma unroll
+                for (int j = 0; j < CW / 4; ++j) v[j] = __ldcg(slot(part) + j * 32);
+#pragma unroll
+                for (int j = 0; j < CW / 4; ++j) {
+                    a[4 * j] += v[j].x;
+                    a[4 * j + 1] += v[j].y;
+                    a[4 * j + 2] += v[j].z;
+                    a[4 * j + 3] += v[j].w;
+                }
+            }
+            return 1;
+        };
         bool finished = false;  // left the loop at the end item (not by giving up on a wait)
         for (uint32_t qi = 0, qph = 0;;) {
             if (!__all_sync(0xffffffffu,
@@ -694,7 +804,21 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
             bool bad = false;
             if constexpr (CHUNKED) {
                 if (main_item) {
-                    if (!consume_chunk_pairs<CW>(acc, nchunks, pairs, abort_flag, p.status)) break;
+                    int kb0, kb1;
+                    unit_stages(p, w.w, nkb, kb0, kb1);
+                    const int unit_chunks = min(2 * kb1, nchunks) - 2 * kb0;
+                    if (!consume_chunk_pairs<CW>(acc, unit_chunks, pairs, abort_flag, p.status)) break;
+                    if (w.w >= 0) {
+                        // A unit of a split tile: the last one of the tile to finish goes on
+                        // with the tile's total in acc; the others are done.
+                        const int last = split_combine(w.w, acc);
+                        if (last < 0) break;
+                        if (last == 0) {
+                            if (!take_staging()) break;
+                            hand_over(tm, tn, kStoreNone, 0);
+                            continue;
+                        }
+                    }
                     // eight independent probe chains (a 64-long chain costs ~300 cycles of
                     // latency at every tile end); NaN in any of them marks the tile
                     float z8[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
@@ -787,6 +911,15 @@ __global__ void __launch_bounds__(TcConfig<BN, EPI_SPLIT, OUT, CHUNKED>::THREADS
                 break;
             const int4 m = ctrl->st_meta[b];
             if (m.z == kStoreEnd) break;
+            if (m.z == kStoreNone) {  // a split unit whose tile another unit finishes: decided, nothing to store
+                if (sw == 0 && lane == 0) {
+                    __threadfence_block();
+                    *main_done = ++decided;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ctrl->st_empty[b]);
+                continue;
+            }
             const int tm = m.x, tn = m.y;
             const int c0 = tn * BN + m.w * Cfg::STAGE_COLS;  // first column of the staged part
             bool redo_queued = false;  // this main tile is redone later in this CTA

@@ -91,11 +91,13 @@ def mm_ex(a, b, out_dtype=torch.float16, chunked=True, *, variant=_lib.VARIANT_A
         raise ValueError("out must be an (M, N) tensor of out_dtype on the operands' device")
     ws_ptr, ws_len = None, 0
     if chunked:
-        need = workspace_bytes(M, N, K)
         if workspace is None:
-            workspace = torch.empty(need, dtype=torch.uint8, device=a.device)
-        elif workspace.numel() < need or workspace.device != a.device or workspace.dtype != torch.uint8:
-            raise ValueError(f"workspace must be a uint8 tensor of at least {need} bytes on the operands' device")
+            workspace = torch.empty(workspace_bytes(M, N, K), dtype=torch.uint8, device=a.device)
+        else:
+            # the flags must fit; the tail split runs only in a workspace_bytes() workspace
+            need = -(-M // 128) * -(-N // 128) * 16
+            if workspace.numel() < need or workspace.device != a.device or workspace.dtype != torch.uint8:
+                raise ValueError(f"workspace must be a uint8 tensor of at least {need} bytes on the operands' device")
         ws_ptr, ws_len = workspace.data_ptr(), workspace.numel()
     dev = _device_index(a)
     stream = _raw_stream(dev)

@@ -66,9 +66,11 @@ extern "C" {
  *   C        device pointer, element (i,j) at C + i*sCm + j*sCn, type c_dtype.
  *   chunked  1: chunked FP16 accumulate + flag + redo (kernel.py:48-49,70-71,75-81);
  *            0: plain FP32 accumulate (kernel.py:50-51).
- *   workspace, ws_bytes  device scratch of at least f16acc_workspace_bytes(M,N,K)
- *            bytes, 16-byte aligned; holds the per-tile overflow flags.  It may
- *            be uninitialised and must stay untouched until the call's work on
+ *   workspace, ws_bytes  device scratch of f16acc_workspace_bytes(M,N,K) bytes,
+ *            16-byte aligned; holds the per-tile overflow flags (16 bytes per
+ *            128x128 tile, the minimum accepted) and the tail split's counters
+ *            and partial tiles (f16acc_set_tail_split).  It may be
+ *            uninitialised and must stay untouched until the call's work on
  *            `stream` is done.  Unused (may be NULL) when chunked == 0.
  *   device   CUDA ordinal that owns A, B, C and the workspace.
  * K == 0 writes zeros; M == 0 or N == 0 does nothing.
@@ -80,7 +82,9 @@ int f16acc_gemm(const void *A, int64_t sAm, int64_t sAk,
                 void *workspace, size_t ws_bytes, int device, void *stream);
 
 /* Bytes of workspace f16acc_gemm needs for an M x N x K product (kernel.py:94-95:
- * sized for the smallest tile any variant uses). */
+ * the flags, sized for the smallest tile any variant uses), plus, when K is
+ * long enough for a tail split, room for its counters and at most 148 FP32
+ * partial tiles of 64 KB (about 9.5 MB). */
 size_t f16acc_workspace_bytes(int64_t M, int64_t N, int64_t K);
 
 /* Static message for a return code (the ValueError texts of kernel.py:87-90). */
@@ -215,6 +219,21 @@ int f16acc_set_schedule(int mode);
 #define F16ACC_FP32_TILES_NARROW 2
 int f16acc_set_fp32_tiles(int mode);
 
+/* Tail split of chunked tcgen05 calls, process-wide, for later calls.  With
+ * F16ACC_TAIL_SPLIT_ON (the default) the tiles past the last full wave of the
+ * SMs (every tile when there are fewer tiles than SMs) are each computed as up
+ * to 4 units over contiguous shares of K, so they spread over the idle SMs; the
+ * unit that finishes last adds the units' FP32 partials in K order (the result
+ * does not depend on which unit that is) and flags the tile on the total.
+ * Within a split tile the FP32 sum is formed per K share and the shares added,
+ * so those tiles can differ from F16ACC_TAIL_SPLIT_OFF in the last bits of the
+ * FP32 sum; flags, redone tiles and every other tile are identical.  The split
+ * needs the workspace size f16acc_workspace_bytes() reports (a workspace that
+ * only holds the flags runs without it).  Returns the previous setting. */
+#define F16ACC_TAIL_SPLIT_OFF 0
+#define F16ACC_TAIL_SPLIT_ON 1
+int f16acc_set_tail_split(int mode);
+
 /* Raw-rate probes, the B200 counterparts of the reference's bench/rate.py and
  * bench/chunkrate.py (measurement aids).  tcgen05 modes: `grid` CTAs (one per
  * SM) each run `chunks` 32-long chunks of 128x128 MMAs on a fixed
@@ -259,7 +278,9 @@ int f16acc_device_status(int device, int reset);
  * before any stream capture on that device.  All calls share the array, which
  * keeps the last call's flags; nothing needs clearing, because every chunked
  * main pass rewrites all flag bytes of the tiles it covers before they are
- * read.  Calls whose work overlaps on the GPU (other streams, other host
+ * read.  The array holds flags only, so these calls run without the tail split
+ * (f16acc_set_tail_split): their results equal f16acc_gemm's with
+ * F16ACC_TAIL_SPLIT_OFF.  Calls whose work overlaps on the GPU (other streams, other host
  * threads) race on the array and must be serialised.  After a kernel gave up
  * on a wait (f16acc_device_status non-zero) the output of that call and the
  * array's flags are undefined until the status word is reset. */
