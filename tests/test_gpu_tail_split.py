@@ -109,9 +109,20 @@ def test_split_tiles_match_unsplit_and_oracle(cuda, M, N, K, layout):
     assert (err <= bound[rows].cpu().numpy()).all()
 
 
-def test_flagged_split_tiles_are_redone_in_fp32(cuda):
+@pytest.mark.parametrize("redo", ["inline", "separate"])
+def test_flagged_split_tiles_are_redone_in_fp32(cuda, redo):
     """Overflowing chunk sums in split tiles flag the tile on the total; the
-    tile is redone over all of K in FP32, bit-equal to chunked=False."""
+    tile is redone over all of K in FP32 (inside the kernel, or by the separate
+    redo launch), bit-equal to chunked=False."""
+    lib = _lib.load()
+    prev = lib.f16acc_set_redo_mode(_lib.REDO_INLINE if redo == "inline" else _lib.REDO_SEPARATE)
+    try:
+        _flagged_split_tiles(cuda)
+    finally:
+        lib.f16acc_set_redo_mode(prev)
+
+
+def _flagged_split_tiles(cuda):
     M, N, K = 2048, 1536, 4096
     g = torch.Generator(device=cuda).manual_seed(17)
     a = torch.randn(M, K, device=cuda, generator=g)
@@ -167,3 +178,20 @@ def test_split_under_both_tile_orders(cuda, schedule):
         finally:
             lib.f16acc_set_schedule(prev)
     assert torch.equal(c, ref)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16], ids=str)
+def test_split_tiles_with_bias_and_narrow_outputs(cuda, out_dtype):
+    """The last unit stages the total like a whole tile: the fused bias and the
+    rounding to a 2-byte C match the unfused product plus y += b bit for bit."""
+    from f16acc_b200.kernel import mm_bias
+
+    M, N, K = 2048, 256, 4096
+    a, b = operands(M, N, K, "w_t", cuda, seed=31)
+    bias = torch.randn(N, device=cuda).half()
+    with tail_split(_lib.TAIL_SPLIT_ON):
+        full = mm(a, b, torch.float32)
+        c = mm(a, b, out_dtype)
+        fused = mm_bias(a, b, bias, out_dtype)
+    assert torch.equal(c, full.to(out_dtype))
+    assert torch.equal(fused, (c.float() + bias.float()).to(out_dtype))
