@@ -180,7 +180,9 @@ int f16acc_set_tc_config(int tile_n, int epi_split);
 /* Cap the SMs a GEMM launch occupies, process-wide, for later calls (0 = all
  * SMs, the default).  The GEMM kernels are persistent (one CTA per SM); a cap
  * leaves SMs free for kernels on other streams, such as an NCCL collective
- * that overlaps a sharded product.  Returns the previous cap. */
+ * that overlaps a sharded product.  The tail split (f16acc_set_tail_split)
+ * plans for the capped SM count, so with it on a cap can change which tiles
+ * are split and the last bits of their FP32 sums.  Returns the previous cap. */
 int f16acc_set_sm_limit(int max_sms);
 
 /* Where a chunked tcgen05 call (f16acc_gemm, _ex, _bias, _allgather,

@@ -195,3 +195,29 @@ def test_split_tiles_with_bias_and_narrow_outputs(cuda, out_dtype):
         fused = mm_bias(a, b, bias, out_dtype)
     assert torch.equal(c, full.to(out_dtype))
     assert torch.equal(fused, (c.float() + bias.float()).to(out_dtype))
+
+
+@pytest.mark.parametrize("M,N,K,caps", [(2048, 256, 4096, (64, 100)), (2048, 1536, 4096, (128,))],
+                         ids=["32_tiles", "192_tiles"])
+def test_split_under_an_sm_cap(cuda, M, N, K, caps):
+    """With f16acc_set_sm_limit the grid is a bounded persistent one in the
+    static order, and the split plans for the capped SM count (32 tiles on 64
+    SMs: 2 parts, on 100: 3; 192 tiles on 128: the last 64 in 2 parts, dealt
+    round robin after the whole ones)."""
+    lib = _lib.load()
+    for cap in caps:
+        assert expected_split(M, N, K, cap)[0] >= 2
+    a, b = operands(M, N, K, "w_t", cuda, seed=41)
+    with tail_split(_lib.TAIL_SPLIT_OFF):
+        off = mm(a, b, torch.float32)
+    bound = chunk_ulp_bound_torch(a, b)
+    for cap in caps:
+        prev = lib.f16acc_set_sm_limit(cap)
+        try:
+            with tail_split(_lib.TAIL_SPLIT_ON):
+                c = mm(a, b, torch.float32)
+                again = mm(a, b, torch.float32)
+        finally:
+            lib.f16acc_set_sm_limit(prev)
+        assert torch.equal(c, again)
+        assert ((c.double() - off.double()).abs() <= bound).all()
