@@ -165,15 +165,16 @@ constexpr int kGroupM = 8;
 // tiles past the last full wave of the SMs (all of them when there are fewer
 // tiles than SMs) run as S units over contiguous shares of K: S = the units
 // that still fit beside each other on the SMs, at most kSplitMax, each unit at
-// least kSplitMinStages 64-wide stages.  A split costs about 8-11 us on the
+// least kSplitMinStages 64-wide stages.  A split costs about 6-8 us on the
 // critical path (the counter reset, each unit's pipeline fill and partial
 // write, the last unit's read-back), measured on shapes from 1024^3 to the
 // Qwen projections, against about 0.39 us per 64-wide stage it takes off a
-// tile; so it is used only when it takes at least kSplitMinSaved stages off.
+// tile; so it is used only when it takes at least kSplitMinSaved stages off
+// (measured break-even: 16-18 stages lose about 1 us, 22-24 gain 2).
 std::atomic<int> g_tail_split{F16ACC_TAIL_SPLIT_ON};
 constexpr int64_t kSplitMax = 4;
 constexpr int64_t kSplitMinStages = 6;
-constexpr int64_t kSplitMinSaved = 32;
+constexpr int64_t kSplitMinSaved = 20;
 constexpr int64_t kSplitSlots = 148;  // partial tiles at most: S x split tiles <= SMs
 constexpr int64_t kSplitPartialBytes = 128 * 128 * 4;
 
@@ -397,7 +398,7 @@ int run(const void* A, int64_t sAm, int64_t sAk, const void* B, int64_t sBk, int
                 p.units = int(units);
                 p.split_cnt = reinterpret_cast<int*>(ws + split_counters_at(M, N));
                 p.split_part = reinterpret_cast<float*>(ws + split_partials_at(M, N));
-                if (cudaMemsetAsync(p.split_cnt, 0, size_t(t.tiles) * sizeof(int), stream) != cudaSuccess)
+                if (launch_zero_split_counters(p.split_cnt, int(t.tiles), stream) != cudaSuccess)
                     return F16ACC_ERR_CUDA;
             }
         }

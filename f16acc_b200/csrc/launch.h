@@ -40,6 +40,10 @@ cudaError_t launch_skinny(const SkinnyParams& p, bool chunked, bool b_kn, int ou
 cudaError_t launch_fill_zero(void* C, int64_t sCm, int64_t sCn, int M, int N, int out, cudaStream_t stream,
                              const __half* bias = nullptr, int64_t sbias = 0);
 
+// Zero the first n tail-split counters ahead of a chunked tcgen05 launch
+// (tc_kernels.cu; programmatic dependent launch on both sides).
+cudaError_t launch_zero_split_counters(int* cnt, int n, cudaStream_t stream);
+
 // Raw-rate probes (rate_probes.cu): mode 0/1 tcgen05 MMA only with an FP16 /
 // FP32 accumulator, mode 2 the chunk-pair pipeline, 30-32 warp-level mma.sync;
 // `out` holds grid * (96 + 128 * epi_split) floats (grid * 256 for 30-32).

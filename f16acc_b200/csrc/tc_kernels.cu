@@ -74,7 +74,32 @@ cudaError_t launch_wide_fp32(const TcParams& p, bool b_mn, int out, int grid, cu
     return cudaErrorInvalidValue;
 }
 
+// Zero the tail split's per-tile counters ahead of the GEMM, as a programmatic
+// dependent launch on both sides: it may start while the previous kernel on
+// the stream drains and writes only after that kernel has completed (the
+// memory may be that kernel's recycled workspace); the GEMM behind it may
+// start its prologue at once and reads the counters only after this kernel
+// has completed.  Unlike a memset, it keeps the overlap between products.
+__global__ void __launch_bounds__(256) zero_split_counters_kernel(int* cnt, int n) {
+    grid_dep_launch();
+    grid_dep_wait();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) cnt[i] = 0;
+}
+
 }  // namespace
+
+cudaError_t launch_zero_split_counters(int* cnt, int n, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, zero_split_counters_kernel, cnt, n);
+}
 
 bool tc_shape_supported(TcShape s) { return s.bn == 128 && (s.epi_split == 2 || s.epi_split == 4); }
 

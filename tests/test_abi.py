@@ -34,16 +34,16 @@ def test_workspace_and_messages():
     lib = _lib.load()
     fb = lib.f16acc_flag_bytes_per_tile()
     assert fb == 16
-    # K too short for a tail split to pay (it must take 32 or more 64-wide
+    # K too short for a tail split to pay (it must take 20 or more 64-wide
     # stages off a tile): the flags alone
     assert lib.f16acc_workspace_bytes(1, 1, 1) == fb
     assert lib.f16acc_workspace_bytes(129, 257, 7) == 2 * 3 * fb
-    assert lib.f16acc_workspace_bytes(4096, 4096, 2624) == 32 * 32 * fb
+    assert lib.f16acc_workspace_bytes(4096, 4096, 1600) == 32 * 32 * fb
     # otherwise the flags, 256-byte aligned, then 148 split counters and 512
     # bytes, then at most 148 partial tiles (4 per tile) of 128 x 128 FP32
     part = 128 * 128 * 4
     assert lib.f16acc_workspace_bytes(4096, 4096, 4096) == 32 * 32 * fb + 148 * 4 + 512 + 148 * part
-    assert lib.f16acc_workspace_bytes(256, 128, 2688) == 256 + 148 * 4 + 512 + 2 * 4 * part
+    assert lib.f16acc_workspace_bytes(256, 128, 1664) == 256 + 148 * 4 + 512 + 2 * 4 * part
     for code in range(6):
         assert lib.f16acc_strerror(code)
     assert b"unknown" in lib.f16acc_strerror(99)

@@ -28,7 +28,7 @@ from tests.helpers import chunk_ulp_bound_torch
 
 pytestmark = pytest.mark.gpu
 
-MIN_STAGES, MAX_SPLIT, MIN_SAVED = 6, 4, 32
+MIN_STAGES, MAX_SPLIT, MIN_SAVED = 6, 4, 20
 
 
 @contextmanager
