@@ -90,3 +90,29 @@ def test_tuning_knobs_validate_and_return_the_previous_setting():
     assert lib.f16acc_set_fp32_tiles(_lib.FP32_TILES_AUTO) == _lib.FP32_TILES_WIDE
     assert lib.f16acc_set_schedule(5) == _lib.ERR_INVALID_ARGUMENT
     assert lib.f16acc_set_redo_mode(5) == _lib.ERR_INVALID_ARGUMENT
+
+
+def test_workspace_bytes_holds_every_tail_split_plan():
+    """Whatever SM count the split plans for (all 148 SMs or a cap), the
+    workspace f16acc_workspace_bytes reports holds the flags, the counters and
+    the partial tiles of that plan, so a caller sizing by it never loses the
+    split.  The plan restated: tiles past the last full wave, S = min(4,
+    SMs / those tiles, stages / 6) parts, used when it takes 20 or more
+    64-wide stages off a tile."""
+    lib = _lib.load()
+    part = 128 * 128 * 4
+    for M in (128, 300, 2048, 8192):
+        for N in (128, 256, 1536, 8960):
+            for K in (1024, 1600, 1664, 4096, 8960):
+                tiles = -(-M // 128) * -(-N // 128)
+                nkb = -(-K // 64)
+                flags = tiles * 16
+                for sms in (148, 132, 100, 64):
+                    r = tiles if tiles < sms else tiles % sms
+                    if r == 0:
+                        continue
+                    s = min(4, sms // r, nkb // 6)
+                    if s < 2 or s * r > 148 or nkb - nkb // s < 20:
+                        continue
+                    need = -(-flags // 256) * 256 + 148 * 4 + 512 + s * r * part
+                    assert lib.f16acc_workspace_bytes(M, N, K) >= need, (M, N, K, sms)
