@@ -34,6 +34,9 @@
 //   last warp   store warp: writes each staged tile out (TMA bulk tensor
 //               stores, or plain stores to a strided C and to the peers) and
 //               makes the in-kernel redo decisions.
+// Chunked mode may split the tiles past the last full wave of the SMs over K
+// (TcParams::split_s): each unit is an ordinary work item over a share of the
+// stages, and the tile's last unit to finish adds the FP32 partials.
 // Every TMA load fills this CTA's own shared memory from this GPU's own memory.
 #pragma once
 
